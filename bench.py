@@ -1,0 +1,374 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 einsum hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+
+A step is one einsum call (one fused launch on the contraction routes) over
+one full BASELINE config, inputs resident in HBM. Under torchrun each rank
+runs its own full-size shard of the batch axis (weak scaling: global batch =
+N x config batch); there is no collective on the data path. Timing: CUDA
+events on the launching stream around exactly K steps, bracketed by a
+barrier and torch.cuda.synchronize(), max over ranks.
+
+Default config is BASELINE config 2 ('bij,bjk->bik' fp16 -> fp32, b=64,
+i=j=k=1024), the contraction the metric is quoted on; --config selects the
+others (names in tests/corpus.py CONFIGS). Inputs are synthetic, seeded.
+
+--impl reference times the reference's own CPU implementation (the libraries
+oracle/build_ref.py compiled from the reference sources, oracle/_ref) on all
+host threads, on bounded slices of the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "pto-einsum_b200"))
+sys.path.insert(0, REPO)
+sys.path.insert(0, os.path.join(REPO, "tests"))
+
+import torch  # noqa: E402
+
+from corpus import CONFIGS  # noqa: E402
+
+CFG = {name: (eq, s0, s1, dt) for name, eq, s0, s1, dt in CONFIGS}
+
+# per config: (metric kind, bound, unit of work per call)
+#   flops = 2*I*L0*L1*C; bytes = inputs read once + fp32 output written once
+def work(name):
+    eq, s0, s1, dt = CFG[name]
+    from pto_einsum import planner
+    r, _ = planner.choose_operand_order("cuda", eq, s0, s1)
+    es = 2 if dt == "float16" else 4
+    n0, n1 = 1, 1
+    for d in s0:
+        n0 *= d
+    for d in s1:
+        n1 *= d
+    nbytes = es * (n0 + n1) + 4 * r["n_elem"]
+    if r["elementwise"] or r["broadcast"]:
+        return dict(kind="bytes", bound="hbm", flops=0, bytes=nbytes, recipe=r)
+    flops = 2 * r["I"] * r["L0"] * r["L1"] * r["C"]
+    bound = "tensor" if name == "cfg2" else "hbm"
+    return dict(kind="flops" if bound == "tensor" else "bytes", bound=bound, flops=flops, bytes=nbytes, recipe=r)
+
+
+def metric_of(w):
+    if w["kind"] == "flops":
+        return "einsum TFLOP/s", "TFLOP/s"
+    return "einsum HBM GB/s", "GB/s"
+
+
+def make_inputs(name, device, rank):
+    eq, s0, s1, dt = CFG[name]
+    dtype = getattr(torch, dt)
+    g = torch.Generator(device="cpu").manual_seed(1000 + rank)
+    if name in ("cfg2",):
+        a = torch.rand(s0, generator=g, dtype=torch.float32)
+        b = torch.rand(s1, generator=g, dtype=torch.float32)
+    elif name == "cfg4b":
+        a = torch.randn(s0, generator=g, dtype=torch.float32)
+        t = torch.arange(s0[0], dtype=torch.float32)
+        diff = t[:, None] - t[None, :]
+        b = torch.where(diff >= 0, torch.pow(torch.tensor(0.99), diff.clamp(min=0)), torch.zeros(()))
+    elif name == "cfg5_rms":
+        a = torch.randn(s0, generator=g)
+        b = torch.rand(s1, generator=g) + 0.5
+    elif name == "cfg5_rope":
+        a = torch.randn(s0, generator=g)
+        S, D = s1
+        pos = torch.arange(S, dtype=torch.float64)[:, None]
+        j = torch.arange(D // 2, dtype=torch.float64)[None, :]
+        ang = pos * torch.pow(10000.0, -2.0 * j / D)
+        b = torch.cat([torch.cos(ang), torch.sin(ang)], dim=1).float()
+    elif name == "cfg5_alibi":
+        a = torch.randn(s0, generator=g)
+        H = s1[0]
+        b = torch.pow(2.0, -8.0 * (torch.arange(H, dtype=torch.float64) + 1) / H).float()
+    else:
+        a = torch.randn(s0, generator=g)
+        b = torch.randn(s1, generator=g)
+    return a.to(dtype).to(device), b.to(dtype).to(device)
+
+
+class Clocks:
+    """Sample nvidia-smi clocks / throttle reasons while the benchmark runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t0, t1):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ts, line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            rows.append((ts, f))
+        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05] or rows
+        sm = [float(f[1]) for _, f in inside if f[1].replace(".", "").isdigit()]
+        mx = [float(f[2]) for _, f in inside if f[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for _, f in inside for k in range(4) if f[5 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(inside)}
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def traffic_of(name):
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(name)
+    return None
+
+
+def cpu_reference(name, seconds_budget=None, threads=None):
+    """Time the reference's compiled CPU library on slices of `name`.
+    Returns (units per second in the config's metric unit, cores, sample text)."""
+    from oracle import ref_cpu
+    if not ref_cpu.available():
+        return None
+    spec_name = next((n for n in ref_cpu.names() if ref_cpu.spec(n)["config"] == name), None)
+    if spec_name is None:
+        return None
+    s = ref_cpu.spec(spec_name)
+    threads = threads or min(os.cpu_count() or 1, 32)
+    a, b = ref_cpu.sample_inputs(spec_name, seed=0)
+    ref_cpu.run(spec_name, a, b)  # warm (loads the library, page-faults the output)
+    outs = [None] * threads
+
+    def worker(k):
+        outs[k] = ref_cpu.run(spec_name, a, b, outs[k])
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=worker, args=(k,)) for k in range(threads)]
+    for t in ths:
+        t.start()
+    for t in ths:
+        t.join()
+    dt = time.perf_counter() - t0
+    w = work(name)
+    frac = 1.0 / s["units"]
+    per_slice = (w["flops"] if w["kind"] == "flops" else w["bytes"]) * frac
+    rate = per_slice * threads / dt / (1e12 if w["kind"] == "flops" else 1e9)
+    sample = (f"{threads} concurrent calls of the reference CPU library for slice {spec_name} "
+              f"({s['equation']} {tuple(s['shape0'])}x{tuple(s['shape1'])}, 1/{s['units']} of {name}), "
+              f"{dt:.2f} s wall")
+    return rate, threads, sample, dt
+
+
+def run_reference_arm(args, rank, world):
+    name = args.config
+    w = work(name)
+    metric, unit = metric_of(w)
+    if rank != 0:
+        return
+    from oracle import ref_cpu
+    if not ref_cpu.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref (reference CPU libraries) not built"}))
+        return
+    threads = min(os.cpu_count() or 1, 32)
+    for _ in range(args.warmup):
+        cpu_reference(name, threads=threads)
+    vals, times = [], []
+    sample = None
+    for _ in range(args.steps):
+        rate, cores, sample, dt = cpu_reference(name, threads=threads)
+        vals.append(rate)
+        times.append(dt)
+    value = statistics.median(vals)
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(times), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": name, "equation": CFG[name][0], "shape0": CFG[name][1],
+                       "shape1": CFG[name][2], "input_dtype": CFG[name][3]},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2", choices=sorted(CFG))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        return
+
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    from pto_einsum import EinsumBuilder, _core
+    name = args.config
+    eq, s0, s1, dt = CFG[name]
+    dtype = getattr(torch, dt)
+    w = work(name)
+    metric, unit = metric_of(w)
+    a, b = make_inputs(name, device, rank)
+    builder = EinsumBuilder(eq, [s0, s1], dtype, device=device)
+    run = builder.build()
+    stream = torch.cuda.current_stream(device)
+
+    for _ in range(args.warmup):
+        out = run(a, b)
+    torch.cuda.synchronize(device)
+    del out
+
+    clocks = Clocks(local)
+    clocks.start()
+    time.sleep(0.2)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    launches0 = _core.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_wall0 = time.time()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(args.steps):
+        evs[k][0].record(stream)
+        out = run(a, b)
+        evs[k][1].record(stream)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    t_wall1 = time.time()
+    if dist:
+        dist.barrier()
+    launches = _core.launch_count() - launches0
+    elapsed_ms = start.elapsed_time(stop)
+    per_launch_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    clk = clocks.stop(t_wall0, t_wall1)
+    if dist:
+        t = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    assert _core.device_error(stream.cuda_stream) == 0, "device error word set"
+
+    units_per_step = w["flops"] if w["kind"] == "flops" else w["bytes"]
+    scale = 1e12 if w["kind"] == "flops" else 1e9
+    value = units_per_step * args.steps * world / (elapsed_ms * 1e-3) / scale
+
+    # ---- end to end through the public API with host buffers ----
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    out_h = torch.empty(w["recipe"]["out_shape"], dtype=torch.float32).pin_memory()
+    del out
+    torch.cuda.synchronize(device)
+    e_steps = max(1, args.e2e_steps)
+    for k in range(e_steps + 1):  # first iteration is a warm-up
+        if k == 1:
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize(device)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        ad = a_h.to(device, non_blocking=True)
+        bd = b_h.to(device, non_blocking=True)
+        o = run(ad, bd)
+        out_h.copy_(o, non_blocking=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_value = units_per_step * e_steps * world / (e2e_ms * 1e-3) / scale
+
+    hbm, tflops, peak_src = peaks()
+    achieved = units_per_step / (per_launch_ms * 1e-3) / scale
+    peak = tflops if w["bound"] == "tensor" else hbm
+    traffic = traffic_of(name)
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            r = cpu_reference(name)
+            if r:
+                cpu = {"value": r[0], "unit": unit, "cores": r[1], "kind": "reference", "sample": r[2]}
+        line = {
+            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dt == "float16" else "f32",
+            "data": "synthetic (seeded)",
+            "config": {"workload": name, "equation": eq, "shape0": s0, "shape1": s1, "input_dtype": dt,
+                       "output_dtype": "float32", "global_batch": s0[0] * world,
+                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "l2": "inputs+output larger than L2 (126 MB)"},
+            "roofline": {"bound": w["bound"], "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s" if w["bound"] == "tensor" else "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": unit,
+                    "h2d_bytes_per_step": a.numel() * a.element_size() + b.numel() * b.element_size(),
+                    "d2h_bytes_per_step": out_h.numel() * 4},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,844 @@
+// pe_gemm.cu - fused contraction: strided TMA loads -> tcgen05/TMEM batched
+// GEMM -> permuted epilogue store, one persistent launch per contraction.
+//
+// Replaces the Ascend mix kernel einsum_fused_kernel (include/pto_einsum.h:65-177)
+// and its batched matmul schedules (include/pto_einsum_matmul.h:115-970):
+//  * Phase A (input permute) becomes TMA addressing: each operand is described
+//    by a rank-5 tensor map over the caller's tensor (free axis, contraction
+//    axis, up to three batch axes, any strides), read K-major or MN-major.
+//    Out-of-range rows/columns/contraction entries arrive as zeros, which is
+//    the K-padding and boundary-tile handling of matmul.h:33-65 without a copy.
+//    Operands a tensor map cannot describe are first gathered by pe_permute.cu
+//    into a canonical [batch, free, K] workspace.
+//  * Phase B is a warp-specialised persistent kernel: warp 0 issues TMA loads
+//    into a STAGES-deep shared-memory ring, one thread of warp 1 issues
+//    tcgen05.mma into a double-buffered TMEM accumulator, warps 2-5 drain the
+//    other accumulator while the next tile is multiplied.
+//  * Phase C (output permute) is fused into the epilogue: tcgen05.ld -> 128B
+//    swizzled staging -> TMA store through a tensor map over the permuted
+//    output, or, when no tensor map fits, strided global stores.
+//  fp16 operands use kind::f16 with fp32 accumulation. fp32 operands use
+//  kind::tf32 in the 3xTF32 scheme: x = big + small with big = x with the low
+//  13 mantissa bits cleared (exactly representable in tf32) and small = x - big;
+//  D += As*Bb + Ab*Bs + Ab*Bb, which restores ~fp32 accuracy. Warps 6-9 do the
+//  split in shared memory between the TMA landing and the MMA.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "pe_common.cuh"
+
+namespace pe {
+
+namespace {
+
+constexpr int kMaxBatchMap = 3;
+
+struct MapBatch {
+    int nb;
+    uint32_t size[kMaxBatchMap];
+    uint32_t div[kMaxBatchMap];
+};
+
+struct Decode {
+    int n;
+    int64_t size[PE_MAX_RANK];
+    int64_t stride[PE_MAX_RANK];
+};
+
+struct GemmArgs {
+    CUtensorMap tma;
+    CUtensorMap tmb;
+    CUtensorMap tmc;
+    int M, N, K;
+    int mblk, nblk, tiles, kiters;
+    int a_mn, b_mn;
+    MapBatch ab, bb, cb;
+    int out_tma;
+    float* out;
+    Decode ob, om, on;
+};
+
+template <int BN_, bool F32_>
+struct Cfg {
+    static constexpr int BM = 128;
+    static constexpr int BN = BN_;
+    static constexpr bool F32 = F32_;
+    static constexpr int ES = F32 ? 4 : 2;
+    static constexpr int BK = 128 / ES;                 // one 128-byte swizzle row
+    static constexpr int MNBOX = 128 / ES;              // MN-major box width
+    static constexpr int A_BYTES = BM * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int TX_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
+    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+    static constexpr int EPI_BYTES = 4 * 2 * 4096;
+    static constexpr int UMMA_K = F32 ? 8 : 16;
+    static constexpr int KSUB = BK / UMMA_K;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int THREADS = F32 ? 320 : 192;
+    static constexpr int NBARS = 3 * STAGES + 5;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+};
+
+__device__ __forceinline__ void batch_coords(const MapBatch& b, uint32_t i, int (&c)[3]) {
+#pragma unroll
+    for (int j = 0; j < kMaxBatchMap; ++j) c[j] = 0;
+    for (int j = 0; j < b.nb; ++j) c[j] = (int)((i / b.div[j]) % b.size[j]);
+}
+
+__device__ __forceinline__ int64_t decode_off(const Decode& d, int64_t x) {
+    if (d.n == 1) return x * d.stride[0];
+    int64_t off = 0;
+    for (int a = d.n - 1; a >= 0; --a) {
+        int64_t q = x / d.size[a];
+        off += (x - q * d.size[a]) * d.stride[a];
+        x = q;
+    }
+    return off;
+}
+
+// Bounded wait that ignores the abort flag: used only while draining.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+    uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > 200000000ull) {
+            record_error(PE_ERR_TIMEOUT | (9 << 8));
+            return;
+        }
+    }
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* epi = smem + C::STAGES * C::STAGE_BYTES;
+    uint64_t* bars = (uint64_t*)(epi + C::EPI_BYTES);
+    uint32_t* tmem_slot = (uint32_t*)(bars + C::NBARS);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const uint32_t bar0 = smem_u32(bars);
+    auto full = [&](int s) { return bar0 + 8u * s; };
+    auto empty = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+    auto split = [&](int s) { return bar0 + 8u * (2 * C::STAGES + s); };
+    auto tfull = [&](int a) { return bar0 + 8u * (3 * C::STAGES + a); };
+    auto tempty = [&](int a) { return bar0 + 8u * (3 * C::STAGES + 2 + a); };
+    const uint32_t mma_done = bar0 + 8u * (3 * C::STAGES + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+            mbar_init(split(s), 128);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 4);
+        }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+        tma_prefetch(&g.tma);
+        tma_prefetch(&g.tmb);
+        if (g.out_tma) tma_prefetch(&g.tmc);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int per_batch = g.mblk * g.nblk;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, issued_par = 0;
+            for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+                const int i = t / per_batch, r = t - i * per_batch;
+                const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
+                int ca[3], cb[3];
+                batch_coords(g.ab, i, ca);
+                batch_coords(g.bb, i, cb);
+                for (int kb = 0; kb < g.kiters; ++kb) {
+                    if (!mbar_wait(empty(stage), phase ^ 1, abort_flag, 1)) break;
+                    uint8_t* sa = smem + stage * C::STAGE_BYTES;
+                    uint8_t* sb = sa + C::A_BYTES;
+                    const int k0 = kb * C::BK;
+                    mbar_arrive_expect_tx(full(stage), C::TX_BYTES);
+                    issued_mask |= 1u << stage;
+                    issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                    if (!g.a_mn) {
+                        tma_load_5d(smem_u32(sa), &g.tma, full(stage), k0, m0, ca[0], ca[1], ca[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < C::BM / C::MNBOX; ++j)
+                            tma_load_5d(smem_u32(sa + j * C::BK * 128), &g.tma, full(stage),
+                                        m0 + j * C::MNBOX, k0, ca[0], ca[1], ca[2]);
+                    }
+                    if (!g.b_mn) {
+                        tma_load_5d(smem_u32(sb), &g.tmb, full(stage), k0, n0, cb[0], cb[1], cb[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < C::BN / C::MNBOX; ++j)
+                            tma_load_5d(smem_u32(sb + j * C::BK * 128), &g.tmb, full(stage),
+                                        n0 + j * C::MNBOX, k0, cb[0], cb[1], cb[2]);
+                    }
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // let every load still in flight land before shared memory is released
+                for (int s = 0; s < C::STAGES; ++s)
+                    if (issued_mask & (1u << s)) drain_wait(full(s), (issued_par >> s) & 1);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            const uint32_t idesc = make_idesc(C::F32 ? 2u : 0u, C::BM, C::BN, g.a_mn, g.b_mn);
+            // byte step of one UMMA_K slice and leading offsets of MN-major tiles
+            const uint32_t a_kstep = g.a_mn ? (C::UMMA_K / 8) * 1024 : 32;
+            const uint32_t b_kstep = g.b_mn ? (C::UMMA_K / 8) * 1024 : 32;
+            const uint32_t a_lbo = g.a_mn ? C::BK * 128 : 16;
+            const uint32_t b_lbo = g.b_mn ? C::BK * 128 : 16;
+            int stage = 0, acc = 0;
+            uint32_t phase = 0, acc_phase = 0;
+            for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+                if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * C::BN);
+                bool ok = true;
+                for (int kb = 0; kb < g.kiters; ++kb) {
+                    if (!mbar_wait(C::F32 ? split(stage) : full(stage), phase, abort_flag, 3)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
+                    const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < C::KSUB; ++ks) {
+                        const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, 1024);
+                        const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+                        if constexpr (C::F32) {
+                            const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, 1024);
+                            const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, 1024);
+                            mma_tf32(d, ads, bd, idesc, accum);
+                            mma_tf32(d, ad, bds, idesc, 1u);
+                            mma_tf32(d, ad, bd, idesc, 1u);
+                        } else {
+                            mma_f16(d, ad, bd, idesc, accum);
+                        }
+                    }
+                    mma_commit(empty(stage));
+                    if (++stage == C::STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(tfull(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1;
+                }
+            }
+            // all MMAs issued by this thread complete before TMEM is released
+            mma_commit(mma_done);
+            drain_wait(mma_done, 0);
+        }
+    } else if (warp < 6) {
+        // ---------------- epilogue: TMEM -> registers -> global ----------------
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        int acc = 0, buf = 0;
+        uint32_t acc_phase = 0;
+        uint8_t* stage_buf = epi + q * 8192;
+        for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+            const int i = t / per_batch, r = t - i * per_batch;
+            const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
+            if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BN);
+            const int mrow = m0 + q * 32;
+            const int m = mrow + lane;
+            int cc[3];
+            batch_coords(g.cb, i, cc);
+            int64_t row_off = 0;
+            if (!g.out_tma && m < g.M) row_off = decode_off(g.ob, i) + decode_off(g.om, m);
+#pragma unroll 1
+            for (int c = 0; c < C::BN / 32; ++c) {
+                const int nc = n0 + c * 32;
+                if (nc >= g.N) break;
+                uint32_t v[32];
+                tmem_ld32(tbase + c * 32, v);
+                tmem_ld_wait();
+                if (g.out_tma) {
+                    uint8_t* sbuf = stage_buf + buf * 4096;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                    uint8_t* row = sbuf + lane * 128;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        uint4 w = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                        *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = w;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && mrow < g.M) {
+                        tma_store_5d(&g.tmc, smem_u32(sbuf), nc, mrow, cc[0], cc[1], cc[2]);
+                        bulk_commit();
+                    }
+                    buf ^= 1;
+                } else if (m < g.M) {
+                    float* o = g.out + row_off;
+#pragma unroll 4
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = nc + j;
+                        if (n < g.N) o[decode_off(g.on, n)] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1;
+            }
+        }
+        if (lane == 0) bulk_wait<0>();
+    } else if constexpr (C::F32) {
+        // ---------------- 3xTF32 split: x -> big (in place) + small ----------------
+        const int st = threadIdx.x - 192;
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+            bool ok = true;
+            for (int kb = 0; kb < g.kiters; ++kb) {
+                if (!mbar_wait(full(stage), phase, abort_flag, 5)) {
+                    ok = false;
+                    break;
+                }
+                uint4* big = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
+                uint4* small = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES + C::TX_BYTES);
+#pragma unroll 4
+                for (int j = st; j < C::TX_BYTES / 16; j += 128) {
+                    uint4 x = big[j];
+                    uint4 h = make_uint4(x.x & 0xFFFFE000u, x.y & 0xFFFFE000u, x.z & 0xFFFFE000u,
+                                         x.w & 0xFFFFE000u);
+                    float4 s = make_float4(__uint_as_float(x.x) - __uint_as_float(h.x),
+                                           __uint_as_float(x.y) - __uint_as_float(h.y),
+                                           __uint_as_float(x.z) - __uint_as_float(h.z),
+                                           __uint_as_float(x.w) - __uint_as_float(h.w));
+                    big[j] = h;
+                    small[j] = *reinterpret_cast<uint4*>(&s);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(split(stage));
+                if (++stage == C::STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            if (!ok) break;
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
+
+struct Axis {
+    int64_t size, stride;
+};
+
+// Drop size-1 axes and merge neighbours that are contiguous in memory
+// (outer.stride == inner.stride * inner.size). Axes are outermost first.
+int coalesce(const Axis* in, int n, Axis* out) {
+    int k = 0;
+    for (int a = 0; a < n; ++a) {
+        if (in[a].size == 1) continue;
+        if (k > 0 && out[k - 1].stride == in[a].stride * in[a].size) {
+            out[k - 1].size *= in[a].size;
+            out[k - 1].stride = in[a].stride;
+        } else {
+            out[k++] = in[a];
+        }
+    }
+    return k;
+}
+
+// Joint coalescing of the batch axes of one map: batch index order is kept.
+struct OperandView {
+    bool direct = false;
+    bool mn_major = false;
+    const void* base = nullptr;
+    int64_t mn_size = 1, mn_stride = 0, k_size = 1, k_stride = 0;
+    int nb = 0;
+    int64_t b_size[kMaxBatchMap] = {1, 1, 1}, b_stride[kMaxBatchMap] = {0, 0, 0};
+};
+
+inline bool al16(int64_t bytes) { return (bytes & 15) == 0; }
+
+// Describe one operand (axes already split into batch / free / contract groups)
+// as a tensor-map-readable view, if possible.
+OperandView view_direct(const void* base, int es, const Axis* batch, int nb, const Axis* fr, int nf,
+                        const Axis* ct, int nc) {
+    OperandView v;
+    v.base = base;
+    if (((uintptr_t)base & 15) != 0) return v;
+    Axis m[PE_MAX_RANK], k[PE_MAX_RANK], b[PE_MAX_RANK];
+    int nm = coalesce(fr, nf, m), nk = coalesce(ct, nc, k), nbb = coalesce(batch, nb, b);
+    if (nm > 1 || nk > 1 || nbb > kMaxBatchMap) return v;
+    if (nm == 1) { v.mn_size = m[0].size; v.mn_stride = m[0].stride; }
+    if (nk == 1) { v.k_size = k[0].size; v.k_stride = k[0].stride; }
+    for (int j = 0; j < nbb; ++j) {
+        if (!al16(b[j].stride * es)) return v;
+        v.b_size[j] = b[j].size;
+        v.b_stride[j] = b[j].stride;
+    }
+    v.nb = nbb;
+    const bool k_unit = v.k_size == 1 || v.k_stride == 1;
+    const bool m_unit = v.mn_size == 1 || v.mn_stride == 1;
+    const bool m_al = v.mn_size == 1 || al16(v.mn_stride * es);
+    const bool k_al = v.k_size == 1 || al16(v.k_stride * es);
+    if (k_unit && m_al) {
+        v.mn_major = false;
+    } else if (m_unit && k_al) {
+        v.mn_major = true;
+    } else {
+        return v;
+    }
+    if (v.mn_size > 0xFFFFFFFFll || v.k_size > 0xFFFFFFFFll) return v;
+    v.direct = true;
+    return v;
+}
+
+// Rank-5 tensor map of an operand view: dims {inner, outer, batch0..2}.
+bool encode_operand(CUtensorMap* tm, const OperandView& v, bool f32, int box_mn_rows) {
+    auto enc = get_encode();
+    if (!enc) return false;
+    const int es = f32 ? 4 : 2;
+    cuuint64_t dims[5];
+    cuuint64_t strides[4];
+    cuuint32_t box[5] = {0, 0, 1, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const int bk = 128 / es;
+    if (!v.mn_major) {
+        dims[0] = (cuuint64_t)v.k_size;
+        dims[1] = (cuuint64_t)v.mn_size;
+        strides[0] = (cuuint64_t)((v.mn_size == 1 ? 1 : v.mn_stride) * es);
+        box[0] = bk;
+        box[1] = box_mn_rows;
+    } else {
+        dims[0] = (cuuint64_t)v.mn_size;
+        dims[1] = (cuuint64_t)v.k_size;
+        strides[0] = (cuuint64_t)((v.k_size == 1 ? 1 : v.k_stride) * es);
+        box[0] = bk;
+        box[1] = bk;
+    }
+    int64_t ext = 16;  // any valid stride for padded size-1 dims
+    for (int j = 0; j < kMaxBatchMap; ++j) {
+        dims[2 + j] = (cuuint64_t)(j < v.nb ? v.b_size[j] : 1);
+        if (j < v.nb) {
+            strides[1 + j] = (cuuint64_t)(v.b_stride[j] * es);
+            int64_t e = v.b_stride[j] * es * v.b_size[j];
+            if (e > ext) ext = e;
+        }
+    }
+    {
+        int64_t e = (int64_t)strides[0] * (int64_t)dims[1];
+        if (e > ext) ext = e;
+    }
+    ext = (ext + 15) & ~(int64_t)15;
+    for (int j = v.nb; j < kMaxBatchMap; ++j) strides[1 + j] = (cuuint64_t)ext;
+    // size-1 outer dim: its stride is unused, make it valid
+    if (dims[1] == 1) strides[0] = (cuuint64_t)ext;
+    for (int j = 0; j < 4; ++j)
+        if ((strides[j] & 15) || strides[j] >= (1ull << 40)) return false;
+    CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                     const_cast<void*>(v.base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+MapBatch map_batch(const OperandView& v) {
+    MapBatch b{};
+    b.nb = v.nb;
+    uint64_t run = 1;
+    for (int j = v.nb - 1; j >= 0; --j) {
+        b.size[j] = (uint32_t)v.b_size[j];
+        b.div[j] = (uint32_t)run;
+        run *= (uint64_t)v.b_size[j];
+    }
+    return b;
+}
+
+// Output: interp axes (batch, free0, free1) with strides of the permuted output.
+struct OutView {
+    Axis b[PE_MAX_RANK], m[PE_MAX_RANK], n[PE_MAX_RANK];
+    int nb, nm, nn;
+};
+
+bool encode_output(CUtensorMap* tm, float* out, const OutView& o, MapBatch* mb) {
+    auto enc = get_encode();
+    if (!enc || ((uintptr_t)out & 15)) return false;
+    Axis m[PE_MAX_RANK], n[PE_MAX_RANK], b[PE_MAX_RANK];
+    int nm = coalesce(o.m, o.nm, m), nn = coalesce(o.n, o.nn, n), nbb = coalesce(o.b, o.nb, b);
+    if (nm > 1 || nn > 1 || nbb > kMaxBatchMap) return false;
+    if (nn == 1 && n[0].stride != 1) return false;
+    if (nm == 1 && !al16(m[0].stride * 4)) return false;
+    cuuint64_t dims[5] = {(cuuint64_t)(nn ? n[0].size : 1), (cuuint64_t)(nm ? m[0].size : 1), 1, 1, 1};
+    cuuint64_t strides[4];
+    int64_t ext = 16;
+    strides[0] = (cuuint64_t)(nm ? m[0].stride * 4 : 16);
+    ext = std::max<int64_t>(ext, (int64_t)strides[0] * (int64_t)dims[1]);
+    OperandView tmp;
+    tmp.nb = nbb;
+    for (int j = 0; j < nbb; ++j) {
+        if (!al16(b[j].stride * 4)) return false;
+        dims[2 + j] = (cuuint64_t)b[j].size;
+        strides[1 + j] = (cuuint64_t)(b[j].stride * 4);
+        ext = std::max<int64_t>(ext, b[j].stride * 4 * b[j].size);
+        tmp.b_size[j] = b[j].size;
+    }
+    ext = (ext + 15) & ~(int64_t)15;
+    for (int j = nbb; j < kMaxBatchMap; ++j) strides[1 + j] = (cuuint64_t)ext;
+    if (dims[1] == 1) strides[0] = (cuuint64_t)ext;
+    for (int j = 0; j < 4; ++j)
+        if ((strides[j] & 15) || strides[j] >= (1ull << 40)) return false;
+    cuuint32_t box[5] = {32, 32, 1, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, out, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return false;
+    *mb = map_batch(tmp);
+    return true;
+}
+
+Decode make_decode(const Axis* ax, int n) {
+    Decode d{};
+    Axis c[PE_MAX_RANK];
+    int k = coalesce(ax, n, c);
+    if (k == 0) {
+        d.n = 1;
+        d.size[0] = 1;
+        d.stride[0] = 0;
+        return d;
+    }
+    d.n = k;
+    for (int a = 0; a < k; ++a) {
+        d.size[a] = c[a].size;
+        d.stride[a] = c[a].stride;
+    }
+    return d;
+}
+
+template <class C>
+int launch_gemm(GemmArgs& g, cudaStream_t s) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM);
+    });
+    if (attr_err != cudaSuccess) return check_cuda(attr_err);
+    g.mblk = (int)((g.M + C::BM - 1) / C::BM);
+    g.nblk = (int)((g.N + C::BN - 1) / C::BN);
+    g.kiters = (int)((g.K + C::BK - 1) / C::BK);
+    int64_t tiles = (int64_t)g.mblk * g.nblk * (int64_t)g.tiles;  // g.tiles holds I on entry
+    if (tiles > 0x7FFFFFFF) return set_last_error(PE_ERR_UNSUPPORTED);
+    g.tiles = (int)tiles;
+    int grid = std::min<int64_t>(tiles, num_sms());
+    gemm_kernel<C><<<grid, C::THREADS, C::SMEM, s>>>(g);
+    count_launch();
+    return check_cuda(cudaGetLastError());
+}
+
+struct Lowered {
+    OperandView a, b;
+    bool a_ws = false, b_ws = false;
+    int64_t kpad = 0;             // padded row length of workspace operands
+    size_t a_off = 0, b_off = 0, ws_bytes = 0;
+    // group axes
+    Axis a_batch[PE_MAX_RANK], a_free[PE_MAX_RANK], a_ct[PE_MAX_RANK];
+    Axis b_batch[PE_MAX_RANK], b_free[PE_MAX_RANK], b_ct[PE_MAX_RANK];
+    int nb = 0, n0 = 0, n1 = 0, nc = 0;
+    OutView out;
+};
+
+bool valid_perm(const int32_t* p, int n) {
+    bool seen[PE_MAX_RANK] = {false};
+    for (int a = 0; a < n; ++a) {
+        if (p[a] < 0 || p[a] >= n || seen[p[a]]) return false;
+        seen[p[a]] = true;
+    }
+    return true;
+}
+
+int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered* L) {
+    if (!pl || (pl->dtype != PE_F32 && pl->dtype != PE_F16)) return PE_ERR_INVALID;
+    const int nb = pl->n_batch, n0 = pl->n_free0, n1 = pl->n_free1, nc = pl->n_contract;
+    if (nb < 0 || n0 < 0 || n1 < 0 || nc < 0) return PE_ERR_INVALID;
+    if (pl->rank0 != nb + n0 + nc || pl->rank1 != nb + nc + n1 || pl->out_rank != nb + n0 + n1 ||
+        pl->rank0 > PE_MAX_RANK || pl->rank1 > PE_MAX_RANK || pl->out_rank > PE_MAX_RANK)
+        return PE_ERR_INVALID;
+    if (!valid_perm(pl->perm0, pl->rank0) || !valid_perm(pl->perm1, pl->rank1) ||
+        !valid_perm(pl->out_perm, pl->out_rank))
+        return PE_ERR_INVALID;
+    const int es = pl->dtype == PE_F32 ? 4 : 2;
+    L->nb = nb;
+    L->n0 = n0;
+    L->n1 = n1;
+    L->nc = nc;
+    int64_t st0[PE_MAX_RANK], st1[PE_MAX_RANK], sto[PE_MAX_RANK], out_shape[PE_MAX_RANK];
+    int64_t run = 1;
+    for (int a = pl->rank0 - 1; a >= 0; --a) { st0[a] = run; run *= pl->shape0[a]; }
+    run = 1;
+    for (int a = pl->rank1 - 1; a >= 0; --a) { st1[a] = run; run *= pl->shape1[a]; }
+    for (int p = 0; p < pl->out_rank; ++p) out_shape[p] = pl->out_interp_shape[pl->out_perm[p]];
+    run = 1;
+    int64_t interp_stride[PE_MAX_RANK];
+    for (int p = pl->out_rank - 1; p >= 0; --p) { sto[p] = run; run *= out_shape[p]; }
+    for (int p = 0; p < pl->out_rank; ++p) interp_stride[pl->out_perm[p]] = sto[p];
+    // group axes (sizes from the raw shapes, consistency with I/L0/L1/C checked)
+    int64_t I = 1, L0 = 1, L1 = 1, C = 1;
+    for (int j = 0; j < nb; ++j) {
+        int a0 = pl->perm0[j], a1 = pl->perm1[j];
+        if (pl->shape0[a0] != pl->shape1[a1]) return PE_ERR_INVALID;
+        L->a_batch[j] = {pl->shape0[a0], st0[a0]};
+        L->b_batch[j] = {pl->shape1[a1], st1[a1]};
+        L->out.b[j] = {pl->shape0[a0], interp_stride[j]};
+        I *= pl->shape0[a0];
+    }
+    for (int j = 0; j < n0; ++j) {
+        int a0 = pl->perm0[nb + j];
+        L->a_free[j] = {pl->shape0[a0], st0[a0]};
+        L->out.m[j] = {pl->shape0[a0], interp_stride[nb + j]};
+        L0 *= pl->shape0[a0];
+    }
+    for (int j = 0; j < nc; ++j) {
+        int a0 = pl->perm0[nb + n0 + j], a1 = pl->perm1[nb + j];
+        if (pl->shape0[a0] != pl->shape1[a1]) return PE_ERR_INVALID;
+        L->a_ct[j] = {pl->shape0[a0], st0[a0]};
+        L->b_ct[j] = {pl->shape1[a1], st1[a1]};
+        C *= pl->shape0[a0];
+    }
+    for (int j = 0; j < n1; ++j) {
+        int a1 = pl->perm1[nb + nc + j];
+        L->b_free[j] = {pl->shape1[a1], st1[a1]};
+        L->out.n[j] = {pl->shape1[a1], interp_stride[nb + n0 + j]};
+        L1 *= pl->shape1[a1];
+    }
+    L->out.nb = nb;
+    L->out.nm = n0;
+    L->out.nn = n1;
+    if (I != pl->I || L0 != pl->L0 || L1 != pl->L1 || C != pl->C) return PE_ERR_INVALID;
+    if (L0 > 0x7FFFFFFFll || L1 > 0x7FFFFFFFll || C > 0x7FFFFFFFll || I > 0xFFFFFFFFll)
+        return PE_ERR_UNSUPPORTED;
+    L->a = view_direct(in0, es, L->a_batch, nb, L->a_free, n0, L->a_ct, nc);
+    L->b = view_direct(in1, es, L->b_batch, nb, L->b_free, n1, L->b_ct, nc);
+    // validate tensor maps now so a rejected layout falls back to the workspace
+    if (L->a.direct && in0) {
+        CUtensorMap t;
+        if (!encode_operand(&t, L->a, es == 4, 128)) L->a.direct = false;
+    }
+    if (L->b.direct && in1) {
+        CUtensorMap t;
+        if (!encode_operand(&t, L->b, es == 4, 128)) L->b.direct = false;
+    }
+    L->a_ws = !L->a.direct;
+    L->b_ws = !L->b.direct;
+    const int64_t vec = 16 / es;
+    L->kpad = ((C > 0 ? C : 1) + vec - 1) / vec * vec;
+    size_t off = 0;
+    if (L->a_ws) {
+        L->a_off = off;
+        off += ((size_t)I * L0 * L->kpad * es + 255) & ~(size_t)255;
+    }
+    if (L->b_ws) {
+        L->b_off = off;
+        off += ((size_t)I * L1 * L->kpad * es + 255) & ~(size_t)255;
+    }
+    L->ws_bytes = off;
+    return PE_OK;
+}
+
+// Gather one operand into the canonical [I, L, Kpad] K-major workspace.
+int gather_canonical(int es, const void* src, void* dst, const Axis* batch, int nb, const Axis* fr,
+                     int nf, const Axis* ct, int nc, int64_t L, int64_t kpad, cudaStream_t s) {
+    int64_t size[PE_MAX_RANK], sst[PE_MAX_RANK], dst_st[PE_MAX_RANK];
+    int nd = 0;
+    // destination strides: contract axes contiguous, free axes x kpad, batch x L*kpad
+    int64_t run = 1;
+    int64_t dst_ct[PE_MAX_RANK], dst_fr[PE_MAX_RANK], dst_b[PE_MAX_RANK];
+    for (int j = nc - 1; j >= 0; --j) { dst_ct[j] = run; run *= ct[j].size; }
+    run = kpad;
+    for (int j = nf - 1; j >= 0; --j) { dst_fr[j] = run; run *= fr[j].size; }
+    run = L * kpad;
+    for (int j = nb - 1; j >= 0; --j) { dst_b[j] = run; run *= batch[j].size; }
+    for (int j = 0; j < nb; ++j) { size[nd] = batch[j].size; sst[nd] = batch[j].stride; dst_st[nd++] = dst_b[j]; }
+    for (int j = 0; j < nf; ++j) { size[nd] = fr[j].size; sst[nd] = fr[j].stride; dst_st[nd++] = dst_fr[j]; }
+    for (int j = 0; j < nc; ++j) { size[nd] = ct[j].size; sst[nd] = ct[j].stride; dst_st[nd++] = dst_ct[j]; }
+    return strided_copy_launch(es, nd, size, sst, dst_st, src, dst, s);
+}
+
+OperandView canonical_view(const void* base, int64_t I, int64_t L, int64_t C, int64_t kpad) {
+    OperandView v;
+    v.direct = true;
+    v.mn_major = false;
+    v.base = base;
+    v.mn_size = L;
+    v.mn_stride = kpad;
+    v.k_size = C;
+    v.k_stride = 1;
+    v.nb = I > 1 ? 1 : 0;
+    v.b_size[0] = I;
+    v.b_stride[0] = L * kpad;
+    return v;
+}
+
+int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
+                     float* out, void* ws, cudaStream_t s);
+
+}  // namespace
+
+int contract_workspace_bytes(const pe_contract_plan* plan, size_t* bytes) {
+    if (!bytes) return set_last_error(PE_ERR_INVALID);
+    Lowered L;
+    // Without pointers the direct/workspace decision cannot see the base
+    // alignment; use 16-byte aligned placeholders (torch allocations are).
+    int rc = lower(plan, (const void*)256, (const void*)256, &L);
+    if (rc) return set_last_error(rc);
+    *bytes = L.ws_bytes;
+    return set_last_error(PE_OK);
+}
+
+int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
+             size_t ws_bytes, cudaStream_t s) {
+    Lowered L;
+    int rc = lower(pl, in0, in1, &L);
+    if (rc) return set_last_error(rc);
+    const int64_t n_out = pl->I * pl->L0 * pl->L1;
+    if (n_out == 0) return set_last_error(PE_OK);
+    if (!in0 || !in1 || !out) return set_last_error(PE_ERR_INVALID);
+    if (pl->C == 0) return check_cuda(cudaMemsetAsync(out, 0, (size_t)n_out * 4, s));
+    if (!get_encode()) return set_last_error(PE_ERR_NO_DEVICE);
+    void* tmp_ws = nullptr;
+    if (L.ws_bytes > 0 && (!ws || ws_bytes < L.ws_bytes)) {
+        // The plan-time size assumed 16-byte aligned inputs; a misaligned view
+        // needs a gather the caller did not budget for: take stream-ordered
+        // scratch for this call only.
+        rc = check_cuda(cudaMallocAsync(&tmp_ws, L.ws_bytes, s));
+        if (rc) return rc;
+        ws = tmp_ws;
+    }
+    rc = contract_lowered(pl, L, in0, in1, out, ws, s);
+    if (tmp_ws) {
+        int rc2 = check_cuda(cudaFreeAsync(tmp_ws, s));
+        if (!rc) rc = rc2;
+    }
+    return rc;
+}
+
+namespace {
+int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
+                     float* out, void* ws, cudaStream_t s) {
+    const int es = pl->dtype == PE_F32 ? 4 : 2;
+    int rc = PE_OK;
+    OperandView va = L.a, vb = L.b;
+    if (L.a_ws) {
+        void* dst = (uint8_t*)ws + L.a_off;
+        rc = gather_canonical(es, in0, dst, L.a_batch, L.nb, L.a_free, L.n0, L.a_ct, L.nc, pl->L0,
+                              L.kpad, s);
+        if (rc) return rc;
+        va = canonical_view(dst, pl->I, pl->L0, pl->C, L.kpad);
+    }
+    if (L.b_ws) {
+        void* dst = (uint8_t*)ws + L.b_off;
+        rc = gather_canonical(es, in1, dst, L.b_batch, L.nb, L.b_free, L.n1, L.b_ct, L.nc, pl->L1,
+                              L.kpad, s);
+        if (rc) return rc;
+        vb = canonical_view(dst, pl->I, pl->L1, pl->C, L.kpad);
+    }
+    GemmArgs g;
+    memset(&g, 0, sizeof(g));
+    g.M = (int)pl->L0;
+    g.N = (int)pl->L1;
+    g.K = (int)pl->C;
+    g.a_mn = va.mn_major;
+    g.b_mn = vb.mn_major;
+    g.ab = map_batch(va);
+    g.bb = map_batch(vb);
+    g.out = out;
+    g.out_tma = encode_output(&g.tmc, out, L.out, &g.cb) ? 1 : 0;
+    g.ob = make_decode(L.out.b, L.out.nb);
+    g.om = make_decode(L.out.m, L.out.nm);
+    g.on = make_decode(L.out.n, L.out.nn);
+    g.tiles = (int)pl->I;
+    const bool f32 = pl->dtype == PE_F32;
+    const int nsm = num_sms();
+    if (f32) {
+        if (!encode_operand(&g.tma, va, true, 128) || !encode_operand(&g.tmb, vb, true, 128))
+            return set_last_error(PE_ERR_UNSUPPORTED);
+        return launch_gemm<Cfg<128, true>>(g, s);
+    }
+    const int64_t mblk = (pl->L0 + 127) / 128;
+    const int64_t tiles256 = pl->I * mblk * ((pl->L1 + 255) / 256);
+    const bool wide = pl->L1 > 128 && tiles256 >= nsm;
+    const int bn = wide ? 256 : 128;
+    if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, bn))
+        return set_last_error(PE_ERR_UNSUPPORTED);
+    if (wide) return launch_gemm<Cfg<256, false>>(g, s);
+    return launch_gemm<Cfg<128, false>>(g, s);
+}
+
+}  // namespace
+
+int gemm_device_error(bool clear) {
+    int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+    if (v && clear) cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    return v;
+}
+
+}  // namespace pe

@@ -1,0 +1,203 @@
+"""CUDA path vs the CPU oracle on the reference's parity corpus (GPU)."""
+import ctypes
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from corpus import ATTENTION_CASES, BROADCAST_CASES, CHAIN_CASES, EINSUM_CASES, BATCHED_PARTIAL, case_id
+from gpu_util import TOL, check_close, seeded
+from oracle import oracle
+from pto_einsum import EinsumBuilder, einsum, planner
+from pto_einsum import _core
+
+pytestmark = pytest.mark.gpu
+
+CONTRACTIONS = EINSUM_CASES + ATTENTION_CASES + CHAIN_CASES + BATCHED_PARTIAL
+DTYPES = [torch.float32, torch.float16]
+
+
+def _is_exact(eq, s0, s1):
+    r, _ = planner.choose_operand_order("cuda", eq, s0, s1)
+    return r["elementwise"] or r["broadcast"]
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("eq,s0,s1", CONTRACTIONS + BROADCAST_CASES,
+                         ids=[case_id(*c) for c in CONTRACTIONS + BROADCAST_CASES])
+def test_einsum_matches_oracle(eq, s0, s1, dtype):
+    seed = zlib.crc32(repr((eq, s0, s1)).encode()) % 10000
+    a, b = seeded(s0, dtype, seed), seeded(s1, dtype, seed + 1)
+    out = einsum(eq, a.cuda(), b.cuda())
+    assert out.dtype == torch.float32 and out.device.type == "cuda"
+    ref = oracle.einsum_cpu(eq, a, b)
+    check_close(out, ref, dtype, exact=_is_exact(eq, s0, s1))
+    # torch.einsum tolerance of the reference suite (tests/test_einsum.py:143-154)
+    tol = 1e-4 if dtype == torch.float32 else 1e-2
+    exp = torch.einsum(eq, a.float(), b.float())
+    torch.testing.assert_close(out.cpu(), exp, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("eq,s0,s1", [
+    ("bij, bjk -> bik", (64, 128, 128), (64, 128, 128)),
+    ("bihd, bjhd -> bihj", (2, 128, 16, 128), (2, 128, 16, 128)),
+    ("bihj, bjhd -> bihd", (2, 128, 16, 128), (2, 128, 16, 128)),
+    ("bvhd, bvhe -> bhde", (2, 128, 16, 128), (2, 128, 16, 128)),
+    ("ji, jk -> ik", (512, 500), (512, 64)),
+])
+def test_bit_exact_reruns(eq, s0, s1, dtype):
+    """Race detector (tests/test_einsum.py:245-364): 8 reruns on the same input
+    must be bit-identical."""
+    b = EinsumBuilder(eq, [s0, s1], dtype)
+    run = b.build()
+    x, y = seeded(s0, dtype, 11).cuda(), seeded(s1, dtype, 12).cuda()
+    first = run(x, y).clone()
+    check_close(first, oracle.einsum_cpu(eq, x.cpu(), y.cpu()), dtype)
+    for _ in range(8):
+        assert torch.equal(run(x, y), first)
+    b.cleanup()
+
+
+def test_builder_reuse_workspace():
+    """Persistent workspace reused across calls with fresh data
+    (tests/test_einsum.py:208-241), including a gathered (K != C) operand."""
+    for eq, s0, s1 in [("ij, jk -> ik", (32, 64), (64, 32)), ("bij, bjk -> bik", (8, 16, 20), (8, 20, 64)),
+                       ("bhsc, bcht -> bsht", (2, 8, 16, 20), (2, 20, 8, 24))]:
+        run = EinsumBuilder(eq, [s0, s1], torch.float32).build()
+        for k in range(10):
+            a, b = seeded(s0, torch.float32, 100 + k), seeded(s1, torch.float32, 200 + k)
+            check_close(run(a.cuda(), b.cuda()), oracle.einsum_cpu(eq, a, b), torch.float32)
+
+
+def test_guard_bands_untouched():
+    """Out-of-bounds canary: the output sits between NaN guard bands that must
+    survive every route (elementwise, broadcast, direct GEMM, gathered GEMM,
+    strided epilogue)."""
+    cases = [("ij,jk->ik", (250, 128), (128, 250), torch.float32),
+             ("bshd,bthd->bsht", (2, 64, 4, 32), (2, 96, 4, 32), torch.float16),
+             ("ij,jk->ki", (32, 64), (64, 48), torch.float32),
+             ("ts,ts->ts", (63, 47), (63, 47), torch.float16),
+             ("bshd,sd->bshd", (2, 8, 4, 16), (8, 16), torch.float16),
+             ("bhsc,bhtc->bhst", (2, 4, 16, 130), (2, 4, 256, 130), torch.float32)]
+    guard = 4096
+    for eq, s0, s1, dt in cases:
+        b = EinsumBuilder(eq, [s0, s1], dt)
+        b.build()
+        n = int(np.prod(b.recipe["out_shape"]))
+        buf = torch.full((guard + n + guard,), float("nan"), device="cuda")
+        x, y = seeded(s0, dt, 5).cuda(), seeded(s1, dt, 6).cuda()
+        if b._swap_operands:
+            x, y = y, x
+        stream = torch.cuda.current_stream().cuda_stream
+        ws = b.workspace(x.device, stream)
+        P = ctypes.POINTER
+        b.lib.run_einsum_exec(ctypes.cast(x.data_ptr(), P(b.c_type)), ctypes.cast(y.data_ptr(), P(b.c_type)),
+                              ctypes.cast(buf.data_ptr() + 4 * guard, P(ctypes.c_float)), ctypes.c_void_p(ws),
+                              ctypes.c_void_p(stream))
+        assert b.lib.run_einsum_last_error() == 0
+        torch.cuda.synchronize()
+        assert torch.isnan(buf[:guard]).all() and torch.isnan(buf[guard + n:]).all()
+        assert not torch.isnan(buf[guard:guard + n]).any()
+        b.cleanup()
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+def test_standalone_entry_points(dtype):
+    """run_transpose_inp0/inp1/out and run_batched_matmul
+    (tests/test_matmul.py:24-151): each stage against the oracle."""
+    eq, s0, s1 = "bhsc, bcht -> bsht", (2, 8, 16, 20), (2, 20, 8, 24)
+    b = EinsumBuilder(eq, [s0, s1], dtype)
+    b.build()
+    r = b.recipe
+    x, y = seeded(s0, dtype, 1), seeded(s1, dtype, 2)
+    if b._swap_operands:
+        x, y = y, x
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    P = ctypes.POINTER
+    ptr = lambda t, ct: ctypes.cast(t.data_ptr(), P(ct))  # noqa: E731
+    p0, p1 = r["in_transpose_idxs"]
+    t0 = torch.empty([x.shape[i] for i in p0], dtype=dtype, device="cuda")
+    t1 = torch.empty([y.shape[i] for i in p1], dtype=dtype, device="cuda")
+    xc, yc = x.cuda(), y.cuda()
+    b.lib.run_transpose_inp0(ptr(xc, b.c_type), ptr(t0, b.c_type), stream)
+    b.lib.run_transpose_inp1(ptr(yc, b.c_type), ptr(t1, b.c_type), stream)
+    torch.cuda.synchronize()
+    assert torch.equal(t0.cpu(), x.permute(p0).contiguous())
+    assert torch.equal(t1.cpu(), y.permute(p1).contiguous())
+    I, L0, L1, C = r["I"], r["L0"], r["L1"], r["C"]
+    res = torch.empty((I, L0, L1), dtype=torch.float32, device="cuda")
+    b.lib.run_batched_matmul(ptr(t0, b.c_type), ptr(t1, b.c_type), ptr(res, ctypes.c_float), stream)
+    torch.cuda.synchronize()
+    assert b.lib.run_einsum_last_error() == 0
+    ref_mm = oracle.batched_matmul_cpu(t0.cpu().reshape(I, L0, C), t1.cpu().reshape(I, C, L1))
+    check_close(res, ref_mm, dtype)
+    out = torch.empty(r["out_shape"], dtype=torch.float32, device="cuda")
+    b.lib.run_transpose_out(ptr(res, ctypes.c_float), ptr(out, ctypes.c_float), stream)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), res.cpu().reshape(r["out_interpret_shape"]).permute(r["out_transpose_idxs"]))
+    b.cleanup()
+
+
+TRANSPOSE_CASES = [  # tests/test_transpose.py:108-162 (shape, perm)
+    ((128,), (0,)), ((32, 64), (0, 1)), ((8, 16, 32), (0, 1, 2)), ((4, 8, 16, 32), (0, 1, 2, 3)),
+    ((123,), (0,)), ((17, 35), (0, 1)), ((3, 7, 13), (0, 1, 2)), ((32, 64), (1, 0)), ((16, 16), (1, 0)),
+    ((10, 20), (1, 0)), ((8, 12), (1, 0)), ((256, 256), (1, 0)), ((512, 64), (1, 0)), ((80, 256), (1, 0)),
+    ((144, 208), (1, 0)), ((201, 199), (1, 0)), ((333, 257), (1, 0)), ((257, 257), (1, 0)),
+    ((2, 3, 4, 5), (3, 1, 0, 2)), ((8, 33, 2, 65), (0, 3, 1, 2)),
+]
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("shape,perm", TRANSPOSE_CASES)
+def test_permute_kernel(shape, perm, dtype):
+    lib = _core.core_lib()
+
+    class Plan(ctypes.Structure):
+        _fields_ = [("dtype", ctypes.c_int32), ("dims", ctypes.c_int32),
+                    ("from_shape", ctypes.c_int64 * 8), ("perm", ctypes.c_int32 * 8)]
+    p = Plan()
+    p.dtype = 0 if dtype == torch.float32 else 1
+    p.dims = len(shape)
+    for i, (s, q) in enumerate(zip(shape, perm)):
+        p.from_shape[i] = s
+        p.perm[i] = q
+    x = seeded(shape, dtype, 9).cuda()
+    out = torch.empty([shape[i] for i in perm], dtype=dtype, device="cuda")
+    rc = lib.pe_permute(ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0
+    assert torch.equal(out, x.permute(perm).contiguous())
+
+
+def test_zero_size_and_degenerate():
+    # empty batch -> empty output; zero contraction -> zeros
+    out = einsum("bij,bjk->bik", torch.rand(0, 4, 8, device="cuda"), torch.rand(0, 8, 5, device="cuda"))
+    assert out.shape == (0, 4, 5)
+    out = einsum("ij,jk->ik", torch.rand(4, 0, device="cuda"), torch.rand(0, 5, device="cuda"))
+    assert torch.equal(out, torch.zeros(4, 5, device="cuda"))
+    out = einsum("i,i->", torch.rand(256, device="cuda"), torch.rand(256, device="cuda"))
+    assert out.shape == ()
+
+
+def test_no_device_errors_and_native_launches():
+    before = _core.launch_count()
+    einsum("ij,jk->ik", torch.rand(64, 64, device="cuda"), torch.rand(64, 64, device="cuda"))
+    assert _core.launch_count() > before
+    assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+def test_validation_errors_cuda():
+    a, b = torch.rand(32, 64, device="cuda"), torch.rand(64, 32, device="cuda")
+    with pytest.raises(ValueError, match="Only exactly two operands are supported."):
+        einsum("ij,jk->ik", a)
+    with pytest.raises(ValueError, match="Operands must have the same datatype."):
+        einsum("ij,jk->ik", a, b.to(torch.int32))
+    run = EinsumBuilder("ij,jk->ik", [(32, 64), (64, 32)], torch.float32).build()
+    with pytest.raises(ValueError, match="do not match built shapes"):
+        run(torch.rand(32, 32, device="cuda"), b)
+    with pytest.raises(TypeError, match="do not match built datatype"):
+        run(a, b.half())
+    with pytest.raises(ValueError, match="same CUDA device"):
+        run(a.cpu(), b.cpu())
