@@ -202,13 +202,14 @@ __device__ __forceinline__ void tmem_ld_wait() {
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand tile
 // (tcgen05 "version 1" descriptor): start address, leading / stride byte
 // offsets (16-byte units), layout type 2 = SWIZZLE_128B.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo,
+                                                    uint32_t layout = 2) {
     uint64_t d = 0;
     d |= (uint64_t)((addr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;  // descriptor version for sm_100
-    d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+    d |= (uint64_t)layout << 61;  // 2 = SWIZZLE_128B, 1 = SWIZZLE_128B with 32-byte atoms
     return d;
 }
 

@@ -78,7 +78,10 @@ struct Cfg {
     static constexpr int EPI_BYTES = 4 * 2 * 4096;
     static constexpr int UMMA_K = F32 ? 8 : 16;
     static constexpr int KSUB = BK / UMMA_K;
-    static constexpr int TMEM_COLS = 2 * BN;
+    // fp32: each accumulator buffer holds two BN-column sums (big*big and the
+    // two cross terms), added with one IEEE fp32 add in the epilogue
+    static constexpr int ACC_COLS = F32 ? 2 * BN : BN;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;
     static constexpr int THREADS = F32 ? 320 : 192;
     static constexpr int NBARS = 3 * STAGES + 5;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
@@ -216,12 +219,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const uint32_t b_kstep = g.b_mn ? (C::UMMA_K / 8) * 1024 : 32;
             const uint32_t a_lbo = g.a_mn ? C::BK * 128 : 16;
             const uint32_t b_lbo = g.b_mn ? C::BK * 128 : 16;
+            // MN-major tf32 tiles use the 128B swizzle with 32-byte atoms (swizzle
+            // period 4 rows): layout type 1 and a 512-byte k-group stride.
+            const uint32_t a_lay = (C::F32 && g.a_mn) ? 1u : 2u, b_lay = (C::F32 && g.b_mn) ? 1u : 2u;
+            const uint32_t a_sbo = a_lay == 1 ? 512 : 1024, b_sbo = b_lay == 1 ? 512 : 1024;
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
             for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
                 if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * C::BN);
+                const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC_COLS);
                 bool ok = true;
                 for (int kb = 0; kb < g.kiters; ++kb) {
                     if (!mbar_wait(C::F32 ? split(stage) : full(stage), phase, abort_flag, 3)) {
@@ -233,15 +240,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
                     for (int ks = 0; ks < C::KSUB; ++ks) {
-                        const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, 1024);
-                        const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, 1024);
+                        const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, b_sbo, b_lay);
                         const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
                         if constexpr (C::F32) {
-                            const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, 1024);
-                            const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, 1024);
-                            mma_tf32(d, ads, bd, idesc, accum);
-                            mma_tf32(d, ad, bds, idesc, 1u);
-                            mma_tf32(d, ad, bd, idesc, 1u);
+                            const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                            const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                            mma_tf32(d + C::BN, ads, bd, idesc, accum);
+                            mma_tf32(d + C::BN, ad, bds, idesc, 1u);
+                            mma_tf32(d, ad, bd, idesc, accum);
                         } else {
                             mma_f16(d, ad, bd, idesc, accum);
                         }
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::ACC_COLS);
             const int mrow = m0 + q * 32;
             const int m = mrow + lane;
             int cc[3];
@@ -286,8 +293,18 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 const int nc = n0 + c * 32;
                 if (nc >= g.N) break;
                 uint32_t v[32];
+                __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the store branch
                 tmem_ld32(tbase + c * 32, v);
-                tmem_ld_wait();
+                if constexpr (C::F32) {
+                    uint32_t w[32];
+                    tmem_ld32(tbase + C::BN + c * 32, w);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+                } else {
+                    tmem_ld_wait();
+                }
                 if (g.out_tma) {
                     uint8_t* sbuf = stage_buf + buf * 4096;
                     if (lane == 0) bulk_wait_read<1>();
@@ -362,6 +379,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
 
     __syncthreads();
     if (warp == 1) {
+        __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
@@ -495,7 +513,8 @@ bool encode_operand(CUtensorMap* tm, const OperandView& v, bool f32, int box_mn_
         if ((strides[j] & 15) || strides[j] >= (1ull << 40)) return false;
     CUresult r = enc(tm, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
                      const_cast<void*>(v.base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     (f32 && v.mn_major) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -575,13 +594,20 @@ Decode make_decode(const Axis* ax, int n) {
 
 template <class C>
 int launch_gemm(GemmArgs& g, cudaStream_t s) {
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        C::SMEM);
-    });
-    if (attr_err != cudaSuccess) return check_cuda(attr_err);
+    // the shared-memory opt-in is a per-device function attribute
+    static std::mutex mu;
+    static bool done[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return set_last_error(PE_ERR_CUDA);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!done[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(gemm_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 C::SMEM);
+            if (e != cudaSuccess) return check_cuda(e);
+            done[dev] = true;
+        }
+    }
     g.mblk = (int)((g.M + C::BM - 1) / C::BM);
     g.nblk = (int)((g.N + C::BN - 1) / C::BN);
     g.kiters = (int)((g.K + C::BK - 1) / C::BK);
@@ -760,8 +786,9 @@ int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float
     if (rc) return set_last_error(rc);
     const int64_t n_out = pl->I * pl->L0 * pl->L1;
     if (n_out == 0) return set_last_error(PE_OK);
-    if (!in0 || !in1 || !out) return set_last_error(PE_ERR_INVALID);
+    if (!out) return set_last_error(PE_ERR_INVALID);
     if (pl->C == 0) return check_cuda(cudaMemsetAsync(out, 0, (size_t)n_out * 4, s));
+    if (!in0 || !in1) return set_last_error(PE_ERR_INVALID);
     if (!get_encode()) return set_last_error(PE_ERR_NO_DEVICE);
     void* tmp_ws = nullptr;
     if (L.ws_bytes > 0 && (!ws || ws_bytes < L.ws_bytes)) {
