@@ -58,6 +58,11 @@ struct GemmArgs {
     int a_mn, b_mn;
     MapBatch ab, bb, cb;
     int out_tma;
+    int acc_slots;   // fp32: accumulator slots per tile (1, 2 or 4)
+    int ksplit;      // work units per output tile (split-K), >= 1
+    int kper;        // k-iterations per unit
+    int nbatch;      // I: batch count of the plan (split-K partials use batch i + sp*I)
+    int raw_big;     // fp32: feed x unmasked as the big part (tensor core truncation)
     float* out;
     Decode ob, om, on;
 };
@@ -80,19 +85,24 @@ struct Cfg {
     static constexpr int KSUB = BK / UMMA_K;
     // fp32: each accumulator buffer holds two BN-column sums (big*big and the
     // two cross terms), added with one IEEE fp32 add in the epilogue
-    static constexpr int ACC_COLS = F32 ? 2 * BN : BN;
-    static constexpr int TMEM_COLS = 2 * ACC_COLS;
+    // TMEM holds 4 (fp32) or 2 (fp16) BN-column slots. fp16: two accumulator
+    // buffers of one slot. fp32: the k-steps of a tile rotate over acc_slots
+    // (S = 1, 2 or 4) slots that the epilogue adds with IEEE fp32 adds, and
+    // 4 / S buffers alternate between tiles.
+    static constexpr int SLOTS = F32 ? 4 : 2;
+    static constexpr int TMEM_COLS = SLOTS * BN;
     static constexpr int THREADS = F32 ? 320 : 192;
-    static constexpr int NBARS = 3 * STAGES + 5;
+    static constexpr int NBARS = 3 * STAGES + 9;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
 };
 
+// Batch coordinates of flat batch index i in one map (fully unrolled so the
+// coordinates stay in registers).
 __device__ __forceinline__ void batch_coords(const MapBatch& b, uint32_t i, int (&c)[3]) {
 #pragma unroll
-    for (int j = 0; j < kMaxBatchMap; ++j) c[j] = 0;
-    for (int j = 0; j < b.nb; ++j) c[j] = (int)((i / b.div[j]) % b.size[j]);
+    for (int j = 0; j < kMaxBatchMap; ++j) c[j] = j < b.nb ? (int)((i / b.div[j]) % b.size[j]) : 0;
 }
 
 __device__ __forceinline__ int64_t decode_off(const Decode& d, int64_t x) {
@@ -131,8 +141,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     auto empty = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
     auto split = [&](int s) { return bar0 + 8u * (2 * C::STAGES + s); };
     auto tfull = [&](int a) { return bar0 + 8u * (3 * C::STAGES + a); };
-    auto tempty = [&](int a) { return bar0 + 8u * (3 * C::STAGES + 2 + a); };
-    const uint32_t mma_done = bar0 + 8u * (3 * C::STAGES + 4);
+    auto tempty = [&](int a) { return bar0 + 8u * (3 * C::STAGES + 4 + a); };
+    const uint32_t mma_done = bar0 + 8u * (3 * C::STAGES + 8);
+    const int S = C::F32 ? g.acc_slots : 1;     // accumulator slots per tile
+    const int NBUF = C::SLOTS / S;              // accumulator buffers
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -141,7 +153,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             mbar_init(empty(s), 1);
             mbar_init(split(s), 128);
         }
-        for (int a = 0; a < 2; ++a) {
+        for (int a = 0; a < 4; ++a) {
             mbar_init(tfull(a), 1);
             mbar_init(tempty(a), 4);
         }
@@ -168,13 +180,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_par = 0;
-            for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+            for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+                const int t = u / g.ksplit, sp = u - t * g.ksplit;
+                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
                 const int i = t / per_batch, r = t - i * per_batch;
                 const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
                 int ca[3], cb[3];
                 batch_coords(g.ab, i, ca);
                 batch_coords(g.bb, i, cb);
-                for (int kb = 0; kb < g.kiters; ++kb) {
+                for (int kb = kb_lo; kb < kb_hi; ++kb) {
                     if (!mbar_wait(empty(stage), phase ^ 1, abort_flag, 1)) break;
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     uint8_t* sb = sa + C::A_BYTES;
@@ -225,12 +239,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const uint32_t a_sbo = a_lay == 1 ? 512 : 1024, b_sbo = b_lay == 1 ? 512 : 1024;
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+            for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+                const int t = u / g.ksplit, sp = u - t * g.ksplit;
+                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
                 if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
                 tc_fence_after();
-                const uint32_t d = tmem_base + (uint32_t)(acc * C::ACC_COLS);
+                const uint32_t dbuf = tmem_base + (uint32_t)(acc * S * C::BN);
                 bool ok = true;
-                for (int kb = 0; kb < g.kiters; ++kb) {
+                for (int kb = kb_lo; kb < kb_hi; ++kb) {
                     if (!mbar_wait(C::F32 ? split(stage) : full(stage), phase, abort_flag, 3)) {
                         ok = false;
                         break;
@@ -238,17 +254,19 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::A_BYTES;
+                    const int slot = C::F32 ? (kb - kb_lo) % S : 0;
+                    const uint32_t d = dbuf + (uint32_t)(slot * C::BN);
 #pragma unroll
                     for (int ks = 0; ks < C::KSUB; ++ks) {
                         const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                        const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+                        const uint32_t accum = (kb - kb_lo >= S || ks > 0) ? 1u : 0u;
                         if constexpr (C::F32) {
                             const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                            mma_tf32(d + C::BN, ads, bd, idesc, accum);
-                            mma_tf32(d + C::BN, ad, bds, idesc, 1u);
-                            mma_tf32(d, ad, bd, idesc, accum);
+                            mma_tf32(d, ads, bd, idesc, accum);
+                            mma_tf32(d, ad, bds, idesc, 1u);
+                            mma_tf32(d, ad, bd, idesc, 1u);
                         } else {
                             mma_f16(d, ad, bd, idesc, accum);
                         }
@@ -261,7 +279,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 }
                 if (!ok) break;
                 mma_commit(tfull(acc));
-                if (++acc == 2) {
+                if (++acc == NBUF) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
@@ -276,18 +294,22 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         int acc = 0, buf = 0;
         uint32_t acc_phase = 0;
         uint8_t* stage_buf = epi + q * 8192;
-        for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+        for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+                const int t = u / g.ksplit, sp = u - t * g.ksplit;
+                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             const int i = t / per_batch, r = t - i * per_batch;
             const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::ACC_COLS);
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * S * C::BN);
+            const int nslots = S < kb_hi - kb_lo ? S : kb_hi - kb_lo;
+            const int bidx = i + sp * g.nbatch;  // output batch (split-K: partial slab sp)
             const int mrow = m0 + q * 32;
             const int m = mrow + lane;
             int cc[3];
-            batch_coords(g.cb, i, cc);
+            batch_coords(g.cb, bidx, cc);
             int64_t row_off = 0;
-            if (!g.out_tma && m < g.M) row_off = decode_off(g.ob, i) + decode_off(g.om, m);
+            if (!g.out_tma && m < g.M) row_off = decode_off(g.ob, bidx) + decode_off(g.om, m);
 #pragma unroll 1
             for (int c = 0; c < C::BN / 32; ++c) {
                 const int nc = n0 + c * 32;
@@ -295,15 +317,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 uint32_t v[32];
                 __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the store branch
                 tmem_ld32(tbase + c * 32, v);
+                tmem_ld_wait();
                 if constexpr (C::F32) {
-                    uint32_t w[32];
-                    tmem_ld32(tbase + C::BN + c * 32, w);
-                    tmem_ld_wait();
+                    for (int sl = 1; sl < nslots; ++sl) {
+                        uint32_t w[32];
+                        tmem_ld32(tbase + (uint32_t)(sl * C::BN) + c * 32, w);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
-                } else {
-                    tmem_ld_wait();
+                        for (int j = 0; j < 32; ++j)
+                            v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+                    }
                 }
                 if (g.out_tma) {
                     uint8_t* sbuf = stage_buf + buf * 4096;
@@ -324,7 +347,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     buf ^= 1;
                 } else if (m < g.M) {
                     float* o = g.out + row_off;
-#pragma unroll 4
+#pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const int n = nc + j;
                         if (n < g.N) o[decode_off(g.on, n)] = __uint_as_float(v[j]);
@@ -334,7 +357,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty(acc));
-            if (++acc == 2) {
+            if (++acc == NBUF) {
                 acc = 0;
                 acc_phase ^= 1;
             }
@@ -345,9 +368,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int st = threadIdx.x - 192;
         int stage = 0;
         uint32_t phase = 0;
-        for (int t = blockIdx.x; t < g.tiles && !*abort_flag; t += gridDim.x) {
+        for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+                const int t = u / g.ksplit, sp = u - t * g.ksplit;
+                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             bool ok = true;
-            for (int kb = 0; kb < g.kiters; ++kb) {
+            for (int kb = kb_lo; kb < kb_hi; ++kb) {
                 if (!mbar_wait(full(stage), phase, abort_flag, 5)) {
                     ok = false;
                     break;
@@ -363,7 +388,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                                            __uint_as_float(x.y) - __uint_as_float(h.y),
                                            __uint_as_float(x.z) - __uint_as_float(h.z),
                                            __uint_as_float(x.w) - __uint_as_float(h.w));
-                    big[j] = h;
+                    if (!g.raw_big) big[j] = h;
                     small[j] = *reinterpret_cast<uint4*>(&s);
                 }
                 fence_proxy_async_smem();
@@ -611,20 +636,57 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
     g.mblk = (int)((g.M + C::BM - 1) / C::BM);
     g.nblk = (int)((g.N + C::BN - 1) / C::BN);
     g.kiters = (int)((g.K + C::BK - 1) / C::BK);
+    if (g.ksplit <= 1 || g.kiters < 2) {
+        g.ksplit = 1;
+        g.kper = g.kiters;
+    } else {
+        g.kper = (g.kiters + g.ksplit - 1) / g.ksplit;
+        g.ksplit = (g.kiters + g.kper - 1) / g.kper;  // every unit gets >= 1 k-iteration
+    }
     int64_t tiles = (int64_t)g.mblk * g.nblk * (int64_t)g.tiles;  // g.tiles holds I on entry
     if (tiles > 0x7FFFFFFF) return set_last_error(PE_ERR_UNSUPPORTED);
     g.tiles = (int)tiles;
-    int grid = std::min<int64_t>(tiles, num_sms());
+    int grid = std::min<int64_t>(tiles * g.ksplit, num_sms());
     gemm_kernel<C><<<grid, C::THREADS, C::SMEM, s>>>(g);
     count_launch();
     return check_cuda(cudaGetLastError());
 }
 
+// fp32 3xTF32: the tensor core reads only the upper 19 bits of each fp32
+// operand (sign, exponent, 10 mantissa bits) and ignores the low 13, so the
+// TMA-landed x already acts as "big" and only "small" = x - big needs writing.
+// PE_TF32_HW_TRUNC=0 restores the explicit masked write-back; a GPU test pins
+// that both give bit-identical results.
+int raw_big_enabled() {
+    const char* e = getenv("PE_TF32_HW_TRUNC");
+    return (e && e[0] == '0') ? 0 : 1;
+}
+
+// Split-K reduction: out[perm(e)] = sum over sp of part[sp][e] (fixed order,
+// so results are run-to-run identical). e walks the canonical [I, L0, L1]
+// index; `od` decodes it into the permuted output offset.
+__global__ void __launch_bounds__(256) splitk_reduce(const float* __restrict__ part, float* __restrict__ out,
+                                                     int64_t n, int ks, Decode od) {
+    int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (; e < n; e += step) {
+        float acc = part[e];
+        for (int k = 1; k < ks; ++k) acc += part[(int64_t)k * n + e];
+        out[decode_off(od, e)] = acc;
+    }
+}
+
+struct Lowered;
+int splitk_reduce_launch(const float* part, float* out, const Lowered& L, const pe_contract_plan* pl, int ks,
+                         cudaStream_t s);
+
 struct Lowered {
     OperandView a, b;
     bool a_ws = false, b_ws = false;
     int64_t kpad = 0;             // padded row length of workspace operands
-    size_t a_off = 0, b_off = 0, ws_bytes = 0;
+    size_t a_off = 0, b_off = 0, p_off = 0, ws_bytes = 0;
+    int bn = 128;                 // N tile of the chosen kernel
+    int ksplit = 1;               // split-K factor (partials in the workspace when > 1)
     // group axes
     Axis a_batch[PE_MAX_RANK], a_free[PE_MAX_RANK], a_ct[PE_MAX_RANK];
     Axis b_batch[PE_MAX_RANK], b_free[PE_MAX_RANK], b_ct[PE_MAX_RANK];
@@ -725,6 +787,35 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
         L->b_off = off;
         off += ((size_t)I * L1 * L->kpad * es + 255) & ~(size_t)255;
     }
+    // Tile shape and split-K. Thin outputs with long contractions leave SMs
+    // idle; splitting K into `ks` ranges fills them at the price of writing and
+    // re-reading ks fp32 partial slabs. Pick ks minimising
+    // (waves of units / ks) + (partial traffic / input traffic).
+    const int nsm = num_sms();
+    const int64_t mblk = (L0 + 127) / 128;
+    if (es == 2) {
+        const int64_t tiles256 = I * mblk * ((L1 + 255) / 256);
+        L->bn = (L1 > 128 && tiles256 >= nsm) ? 256 : 128;
+    }
+    const int64_t tiles = I * mblk * ((L1 + L->bn - 1) / L->bn);
+    const int64_t kiters = (C + (128 / es) - 1) / (128 / es);
+    if (tiles > 0 && tiles * 2 <= nsm && kiters >= 64) {
+        const double in_bytes = (double)es * (double)C * (double)(I * L0 + I * L1);
+        const double part_bytes = 8.0 * (double)(I * L0 * L1);
+        double best = 1.0;
+        for (int ks = 2; ks <= 16 && ks <= kiters / 8; ++ks) {
+            const double waves = (double)((tiles * ks + nsm - 1) / nsm) / ks;
+            const double cost = waves + ks * part_bytes / in_bytes;
+            if (cost < best - 0.02) {
+                best = cost;
+                L->ksplit = ks;
+            }
+        }
+    }
+    if (L->ksplit > 1) {
+        L->p_off = off;
+        off += ((size_t)L->ksplit * I * L0 * L1 * 4 + 255) & ~(size_t)255;
+    }
     L->ws_bytes = off;
     return PE_OK;
 }
@@ -746,6 +837,24 @@ int gather_canonical(int es, const void* src, void* dst, const Axis* batch, int 
     for (int j = 0; j < nf; ++j) { size[nd] = fr[j].size; sst[nd] = fr[j].stride; dst_st[nd++] = dst_fr[j]; }
     for (int j = 0; j < nc; ++j) { size[nd] = ct[j].size; sst[nd] = ct[j].stride; dst_st[nd++] = dst_ct[j]; }
     return strided_copy_launch(es, nd, size, sst, dst_st, src, dst, s);
+}
+
+int splitk_reduce_launch(const float* part, float* out, const Lowered& L, const pe_contract_plan* pl, int ks,
+                         cudaStream_t s) {
+    Axis ax[3 * PE_MAX_RANK];
+    int n = 0;
+    for (int j = 0; j < L.out.nb; ++j) ax[n++] = L.out.b[j];
+    for (int j = 0; j < L.out.nm; ++j) ax[n++] = L.out.m[j];
+    for (int j = 0; j < L.out.nn; ++j) ax[n++] = L.out.n[j];
+    Axis c[3 * PE_MAX_RANK];
+    int k = coalesce(ax, n, c);
+    if (k > PE_MAX_RANK) return set_last_error(PE_ERR_UNSUPPORTED);
+    Decode od = make_decode(c, k);
+    const int64_t total = pl->I * pl->L0 * pl->L1;
+    int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms() * 8;
+    splitk_reduce<<<(int)std::min(blocks, cap), 256, 0, s>>>(part, out, total, ks, od);
+    count_launch();
+    return check_cuda(cudaGetLastError());
 }
 
 OperandView canonical_view(const void* base, int64_t I, int64_t L, int64_t C, int64_t kpad) {
@@ -836,27 +945,41 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     g.b_mn = vb.mn_major;
     g.ab = map_batch(va);
     g.bb = map_batch(vb);
-    g.out = out;
-    g.out_tma = encode_output(&g.tmc, out, L.out, &g.cb) ? 1 : 0;
-    g.ob = make_decode(L.out.b, L.out.nb);
-    g.om = make_decode(L.out.m, L.out.nm);
-    g.on = make_decode(L.out.n, L.out.nn);
+    g.ksplit = L.ksplit;
+    g.nbatch = (int)pl->I;
+    g.raw_big = raw_big_enabled();
+    OutView slab;  // split-K: canonical partial slabs [ksplit * I, L0, L1]
+    const OutView* ov = &L.out;
+    float* target = out;
+    if (L.ksplit > 1) {
+        slab.nb = slab.nm = slab.nn = 1;
+        slab.b[0] = {(int64_t)L.ksplit * pl->I, pl->L0 * pl->L1};
+        slab.m[0] = {pl->L0, pl->L1};
+        slab.n[0] = {pl->L1, 1};
+        ov = &slab;
+        target = (float*)((uint8_t*)ws + L.p_off);
+    }
+    g.out = target;
+    g.out_tma = encode_output(&g.tmc, target, *ov, &g.cb) ? 1 : 0;
+    g.ob = make_decode(ov->b, ov->nb);
+    g.om = make_decode(ov->m, ov->nm);
+    g.on = make_decode(ov->n, ov->nn);
     g.tiles = (int)pl->I;
     const bool f32 = pl->dtype == PE_F32;
-    const int nsm = num_sms();
     if (f32) {
+        // more slots for long contractions: fewer accumulation steps per slot
+        const int64_t kit = (pl->C + 31) / 32;
+        g.acc_slots = kit >= 32 ? 4 : (kit >= 8 ? 2 : 1);
         if (!encode_operand(&g.tma, va, true, 128) || !encode_operand(&g.tmb, vb, true, 128))
             return set_last_error(PE_ERR_UNSUPPORTED);
-        return launch_gemm<Cfg<128, true>>(g, s);
+        rc = launch_gemm<Cfg<128, true>>(g, s);
+    } else {
+        if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, L.bn))
+            return set_last_error(PE_ERR_UNSUPPORTED);
+        rc = L.bn == 256 ? launch_gemm<Cfg<256, false>>(g, s) : launch_gemm<Cfg<128, false>>(g, s);
     }
-    const int64_t mblk = (pl->L0 + 127) / 128;
-    const int64_t tiles256 = pl->I * mblk * ((pl->L1 + 255) / 256);
-    const bool wide = pl->L1 > 128 && tiles256 >= nsm;
-    const int bn = wide ? 256 : 128;
-    if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, bn))
-        return set_last_error(PE_ERR_UNSUPPORTED);
-    if (wide) return launch_gemm<Cfg<256, false>>(g, s);
-    return launch_gemm<Cfg<128, false>>(g, s);
+    if (rc || L.ksplit <= 1) return rc;
+    return splitk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g.ksplit, s);
 }
 
 }  // namespace

@@ -60,6 +60,50 @@ def test_bit_exact_reruns(eq, s0, s1, dtype):
     b.cleanup()
 
 
+SPLITK_CASES = [  # thin outputs, long contractions: split-K partials + reduce
+    ("ts, sp -> tp", (512, 8192), (8192, 128)),
+    ("ij, jk -> ik", (16, 4096), (4096, 16)),
+    ("bij, bjk -> bik", (2, 128, 8192), (2, 8192, 96)),
+    ("bki, bkj -> ibj", (2, 4096, 64), (2, 4096, 48)),
+]
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("eq,s0,s1", SPLITK_CASES, ids=[case_id(*c) for c in SPLITK_CASES])
+def test_split_k(eq, s0, s1, dtype):
+    b = EinsumBuilder(eq, [s0, s1], dtype)
+    run = b.build()
+    x, y = seeded(s0, dtype, 21, "randn"), seeded(s1, dtype, 22, "randn")
+    first = run(x.cuda(), y.cuda()).clone()
+    check_close(first, oracle.einsum_cpu(eq, x, y), dtype)
+    for _ in range(3):
+        assert torch.equal(run(x.cuda(), y.cuda()), first)
+    b.cleanup()
+
+
+def test_fp32_long_positive_contraction():
+    """All-positive data, K = 8192: the worst case for the tensor core's fp32
+    accumulation (errors do not cancel); 4 interleaved accumulators keep it
+    within the fp32 tolerance."""
+    eq, s0, s1 = "ij, jk -> ik", (256, 8192), (8192, 256)
+    a, b = seeded(s0, torch.float32, 31), seeded(s1, torch.float32, 32)
+    check_close(einsum(eq, a.cuda(), b.cuda()), oracle.einsum_cpu(eq, a, b), torch.float32)
+
+
+def test_tf32_truncation_mode_is_exact(monkeypatch):
+    """The default 3xTF32 split feeds raw fp32 data as the tf32 "big" part
+    (the tensor core ignores the low 13 mantissa bits); it must give the same
+    bits as writing back the explicitly masked value."""
+    for eq, s0, s1 in [("ij, jk -> ik", (256, 1024), (1024, 256)), ("ts, sp -> tp", (512, 4096), (4096, 128)),
+                       ("ji, jk -> ik", (200, 96), (200, 136))]:
+        a, b = seeded(s0, torch.float32, 41, "randn").cuda(), seeded(s1, torch.float32, 42, "randn").cuda()
+        monkeypatch.setenv("PE_TF32_HW_TRUNC", "0")
+        masked = einsum(eq, a, b)
+        monkeypatch.setenv("PE_TF32_HW_TRUNC", "1")
+        raw = einsum(eq, a, b)
+        assert torch.equal(masked, raw)
+
+
 def test_builder_reuse_workspace():
     """Persistent workspace reused across calls with fresh data
     (tests/test_einsum.py:208-241), including a gathered (K != C) operand."""
