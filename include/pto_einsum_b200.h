@@ -111,6 +111,29 @@ void pe_workspace_destroy(void* handle);
 int pe_batched_matmul(int32_t dtype, int64_t I, int64_t L0, int64_t L1, int64_t C,
                       const void* a, const void* b, float* c, void* stream);
 
+/*
+ * Allocation-free contraction (no counterpart in the reference). Same result
+ * as pe_contract, but the scratch it may need (gathered operands, split-K
+ * partial sums) comes from a fixed 32 MiB array compiled into this library
+ * instead of cudaMalloc, for callers that cannot allocate device memory at
+ * call time (fixed memory budgets, foreign allocators, latency-critical
+ * paths). The array occupies 32 MiB on every GPU that uses the library until
+ * the process exits.
+ *  - Plans needing more scratch than pe_noalloc_scratch_bytes() are rejected
+ *    with PE_ERR_WORKSPACE before anything is launched.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress) with that device current; make that first call
+ *    before any stream capture.
+ *  - All calls share the one array: calls whose kernels can overlap on the GPU
+ *    (different streams, or several host threads) race on it and must be
+ *    serialised by the caller. Nothing in it needs to start zeroed; every
+ *    byte a call reads was written earlier by the same call.
+ */
+int pe_contract_noalloc(const pe_contract_plan* plan, const void* in0, const void* in1,
+                        float* out, void* stream);
+/* Size in bytes of the fixed scratch array behind pe_contract_noalloc. */
+size_t pe_noalloc_scratch_bytes(void);
+
 /* ---- streaming multiplies ------------------------------------------------ */
 
 /* Hadamard product out[i] = float(a[i]) * float(b[i]), i < n. */

@@ -14,7 +14,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 INCLUDE = os.path.join(REPO, "include")
 OUT_DIR = os.path.join(PKG, "_lib")
 OUT = os.path.join(OUT_DIR, "libpto_einsum_b200.so")
-SOURCES = ["pe_api.cu", "pe_stream.cu", "pe_permute.cu", "pe_gemm.cu"]
+SOURCES = ["pe_api.cu", "pe_stream.cu", "pe_permute.cu", "pe_gemm.cu", "pe_noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -888,6 +888,15 @@ int contract_workspace_bytes(const pe_contract_plan* plan, size_t* bytes) {
     return set_last_error(PE_OK);
 }
 
+int contract_scratch_bytes(const pe_contract_plan* plan, const void* in0, const void* in1, size_t* bytes) {
+    if (!bytes) return set_last_error(PE_ERR_INVALID);
+    Lowered L;
+    int rc = lower(plan, in0, in1, &L);
+    if (rc) return set_last_error(rc);
+    *bytes = L.ws_bytes;
+    return set_last_error(PE_OK);
+}
+
 int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
              size_t ws_bytes, cudaStream_t s) {
     Lowered L;

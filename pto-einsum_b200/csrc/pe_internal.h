@@ -24,6 +24,8 @@ int strided_copy_launch(int es, int nd, const int64_t* size, const int64_t* sst,
                         const int64_t* dst_st, const void* src, void* dst, cudaStream_t s);
 
 int contract_workspace_bytes(const pe_contract_plan* plan, size_t* bytes);
+// Scratch bytes pe_contract needs for these exact input pointers.
+int contract_scratch_bytes(const pe_contract_plan* plan, const void* in0, const void* in1, size_t* bytes);
 int contract(const pe_contract_plan* plan, const void* in0, const void* in1, float* out, void* ws,
              size_t ws_bytes, cudaStream_t s);
 
