@@ -79,8 +79,11 @@ struct Cfg {
     static constexpr int B_BYTES = BN * 128;
     static constexpr int TX_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
-    static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
-    static constexpr int EPI_BYTES = 4 * 2 * 4096;
+    // epilogue warps (two per TMEM lane quadrant for fp16), 2 x 4 KB staging each
+    static constexpr int EPIW = F32 ? 4 : 8;
+    static constexpr int EBUF = EPIW == 8 ? 1 : 2;   // 4 KB staging buffers per epilogue warp
+    static constexpr int EPI_BYTES = EPIW * EBUF * 4096;
+    static constexpr int STAGES = (224 * 1024 - EPI_BYTES) / STAGE_BYTES;
     static constexpr int UMMA_K = F32 ? 8 : 16;
     static constexpr int KSUB = BK / UMMA_K;
     // fp32: each accumulator buffer holds two BN-column sums (big*big and the
@@ -91,7 +94,7 @@ struct Cfg {
     // 4 / S buffers alternate between tiles.
     static constexpr int SLOTS = F32 ? 4 : 2;
     static constexpr int TMEM_COLS = SLOTS * BN;
-    static constexpr int THREADS = F32 ? 320 : 192;
+    static constexpr int THREADS = 64 + 32 * EPIW + (F32 ? 128 : 0);
     static constexpr int NBARS = 3 * STAGES + 9;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -155,7 +158,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         }
         for (int a = 0; a < 4; ++a) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), 4);
+            mbar_init(tempty(a), C::EPIW);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -288,15 +291,22 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             mma_commit(mma_done);
             drain_wait(mma_done, 0);
         }
-    } else if (warp < 6) {
+    } else if (warp < 2 + C::EPIW) {
         // ---------------- epilogue: TMEM -> registers -> global ----------------
-        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        // Warp w may only read TMEM lanes 32*(w%4)..+31, so the warps sharing a
+        // lane quadrant take alternate 32-column chunks of the tile. The next
+        // chunk's tcgen05.ld is issued before the current chunk is staged
+        // and stored, hiding the TMEM load latency.
+        constexpr int NH = C::EPIW / 4;
+        const int ew = warp - 2;
+        const int q = warp & 3;
+        const int half = ew >> 2;
         int acc = 0, buf = 0;
         uint32_t acc_phase = 0;
-        uint8_t* stage_buf = epi + q * 8192;
+        uint8_t* stage_buf = epi + ew * C::EBUF * 4096;
         for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
-                const int t = u / g.ksplit, sp = u - t * g.ksplit;
-                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
+            const int t = u / g.ksplit, sp = u - t * g.ksplit;
+            const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             const int i = t / per_batch, r = t - i * per_batch;
             const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
@@ -306,18 +316,22 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const int bidx = i + sp * g.nbatch;  // output batch (split-K: partial slab sp)
             const int mrow = m0 + q * 32;
             const int m = mrow + lane;
+            const int nvalid = min(C::BN / 32, (g.N - n0 + 31) / 32);
             int cc[3];
             batch_coords(g.cb, bidx, cc);
             int64_t row_off = 0;
             if (!g.out_tma && m < g.M) row_off = decode_off(g.ob, bidx) + decode_off(g.om, m);
-#pragma unroll 1
-            for (int c = 0; c < C::BN / 32; ++c) {
-                const int nc = n0 + c * 32;
-                if (nc >= g.N) break;
-                uint32_t v[32];
-                __syncwarp();  // tcgen05.ld is .sync.aligned: reconverge after the store branch
-                tmem_ld32(tbase + c * 32, v);
+            uint32_t v[32], vn[32];
+            if (half < nvalid) {
+                __syncwarp();
+                tmem_ld32(tbase + half * 32, v);
                 tmem_ld_wait();
+            }
+#pragma unroll 1
+            for (int c = half; c < nvalid; c += NH) {
+                const int nc = n0 + c * 32;
+                const bool more = c + NH < nvalid;
+                __syncwarp();  // tcgen05.ld / wait::ld are .sync.aligned
                 if constexpr (C::F32) {
                     for (int sl = 1; sl < nslots; ++sl) {
                         uint32_t w[32];
@@ -327,10 +341,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         for (int j = 0; j < 32; ++j)
                             v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
                     }
+                    if (more) tmem_ld32(tbase + (c + NH) * 32, vn);
+                } else {
+                    if (more) tmem_ld32(tbase + (c + NH) * 32, vn);
                 }
                 if (g.out_tma) {
                     uint8_t* sbuf = stage_buf + buf * 4096;
-                    if (lane == 0) bulk_wait_read<1>();
+                    if (lane == 0) {
+                        if constexpr (C::EBUF == 2) bulk_wait_read<1>();
+                        else bulk_wait_read<0>();
+                    }
                     __syncwarp();
                     uint8_t* row = sbuf + lane * 128;
 #pragma unroll
@@ -344,7 +364,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         tma_store_5d(&g.tmc, smem_u32(sbuf), nc, mrow, cc[0], cc[1], cc[2]);
                         bulk_commit();
                     }
-                    buf ^= 1;
+                    if constexpr (C::EBUF == 2) buf ^= 1;
                 } else if (m < g.M) {
                     float* o = g.out + row_off;
 #pragma unroll
@@ -352,6 +372,12 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         const int n = nc + j;
                         if (n < g.N) o[decode_off(g.on, n)] = __uint_as_float(v[j]);
                     }
+                }
+                if (more) {
+                    __syncwarp();
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = vn[j];
                 }
             }
             tc_fence_before();
@@ -365,7 +391,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         if (lane == 0) bulk_wait<0>();
     } else if constexpr (C::F32) {
         // ---------------- 3xTF32 split: x -> big (in place) + small ----------------
-        const int st = threadIdx.x - 192;
+        const int st = threadIdx.x - 32 * (2 + C::EPIW);
         int stage = 0;
         uint32_t phase = 0;
         for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {

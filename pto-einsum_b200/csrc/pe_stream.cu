@@ -30,6 +30,28 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 }
 
 __device__ __forceinline__ float to_f(float x) { return x; }
+
+// Lane l holds the 8 fp32 results of elements [8l, 8l+8) of a warp's
+// 256-element block starting at `base`. Storing them directly would make each
+// 16-byte store instruction cover only half of every 32-byte sector it
+// touches; instead lanes exchange values so that each of the two store
+// instructions writes 512 contiguous bytes (lane l writes elements 4l..4l+3,
+// then 128+4l..).
+__device__ __forceinline__ void store8_coalesced(float* __restrict__ base, const float (&p)[8], int lane) {
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int src = half * 16 + (lane >> 1);
+        const bool hi = lane & 1;
+        float q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float lo_v = __shfl_sync(0xffffffffu, p[k], src);
+            const float hi_v = __shfl_sync(0xffffffffu, p[4 + k], src);
+            q[k] = hi ? hi_v : lo_v;
+        }
+        st_stream(reinterpret_cast<float4*>(base) + half * 32 + lane, make_float4(q[0], q[1], q[2], q[3]));
+    }
+}
 __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
 
 // ---- Hadamard -----------------------------------------------------------------
@@ -50,17 +72,49 @@ __global__ void __launch_bounds__(256) ew_mul_f32_vec(const float4* __restrict__
     }
 }
 
+__device__ __forceinline__ void mul8(const uint4& a, const uint4& b, float (&p)[8]) {
+    float x[8], y[8];
+    unpack8(a, x);
+    unpack8(b, y);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) p[k] = x[k] * y[k];
+}
+
+// Stores the 8 products of vector i: warp-cooperatively when the warp's 32
+// consecutive vectors are all in range, else one thread at a time.
+__device__ __forceinline__ void store8(float* __restrict__ out, int64_t i, int lane, bool full_warp,
+                                       const float (&p)[8]) {
+    if (full_warp) {
+        store8_coalesced(out + (i - lane) * 8, p, lane);
+    } else {
+        float4* o = reinterpret_cast<float4*>(out) + 2 * i;
+        st_stream(o, make_float4(p[0], p[1], p[2], p[3]));
+        st_stream(o + 1, make_float4(p[4], p[5], p[6], p[7]));
+    }
+}
+
 __global__ void __launch_bounds__(256) ew_mul_f16_vec(const uint4* __restrict__ a,
                                                       const uint4* __restrict__ b,
-                                                      float4* __restrict__ out, int64_t nvec) {
+                                                      float* __restrict__ out, int64_t nvec) {
+    const int lane = threadIdx.x & 31;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
-    for (; i < nvec; i += step) {
-        float x[8], y[8];
-        unpack8(ld_stream(a + i), x);
-        unpack8(ld_stream(b + i), y);
-        st_stream(out + 2 * i, make_float4(x[0] * y[0], x[1] * y[1], x[2] * y[2], x[3] * y[3]));
-        st_stream(out + 2 * i + 1, make_float4(x[4] * y[4], x[5] * y[5], x[6] * y[6], x[7] * y[7]));
+    for (; i < nvec; i += 2 * step) {
+        const int64_t i1 = i + step;
+        const bool two = i1 < nvec;
+        const uint4 a0 = ld_stream(a + i), b0 = ld_stream(b + i);
+        uint4 a1 = make_uint4(0, 0, 0, 0), b1 = a1;
+        if (two) {
+            a1 = ld_stream(a + i1);
+            b1 = ld_stream(b + i1);
+        }
+        float p[8];
+        mul8(a0, b0, p);
+        store8(out, i, lane, i - lane + 32 <= nvec, p);
+        if (two) {
+            mul8(a1, b1, p);
+            store8(out, i1, lane, i1 - lane + 32 <= nvec, p);
+        }
     }
 }
 
@@ -94,46 +148,65 @@ __device__ __forceinline__ int64_t outer_base(const BcastParams& p, uint32_t o) 
     return base;
 }
 
+template <typename T>
+__device__ __forceinline__ void bcast_apply(const T* __restrict__ bc, float* __restrict__ out,
+                                            const BcastParams& p, uint32_t v, const uint4& raw, int lane,
+                                            bool full_warp) {
+    constexpr int VEC = 16 / sizeof(T);
+    uint32_t o = fdiv(v, p.inner_v);
+    uint32_t w = v - o * p.inner_v.div;  // vector index inside the group
+    int64_t boff = outer_base(p, o);
+    float x[VEC], y[VEC];
+    if constexpr (sizeof(T) == 4) {
+        x[0] = __uint_as_float(raw.x); x[1] = __uint_as_float(raw.y);
+        x[2] = __uint_as_float(raw.z); x[3] = __uint_as_float(raw.w);
+    } else {
+        unpack8(raw, x);
+    }
+    if (p.mode == 0) {
+        uint32_t c = w - fdiv(w, p.cc_v) * p.cc_v.div;
+        const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(bc + boff + (int64_t)c * VEC));
+        if constexpr (sizeof(T) == 4) {
+            y[0] = __uint_as_float(b4.x); y[1] = __uint_as_float(b4.y);
+            y[2] = __uint_as_float(b4.z); y[3] = __uint_as_float(b4.w);
+        } else {
+            unpack8(b4, y);
+        }
+    } else {
+        float sc = to_f(bc[boff]);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) y[j] = sc;
+    }
+    float r[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) r[j] = x[j] * y[j];
+    if constexpr (VEC == 8) {
+        store8(out, v, lane, full_warp, r);
+    } else {
+        st_stream(reinterpret_cast<float4*>(out) + v, make_float4(r[0], r[1], r[2], r[3]));
+    }
+}
+
 // Vector path: Inner and Cc are multiples of VEC, so a vector never crosses a
 // group and (mode 0) the matching broadcast run is VEC contiguous elements.
+// Each iteration issues two independent 16-byte loads of the full operand
+// before using either, to keep more bytes in flight per thread.
 template <typename T>
 __global__ void __launch_bounds__(256) bcast_mul_vec(const T* __restrict__ full,
                                                      const T* __restrict__ bc,
                                                      float* __restrict__ out, BcastParams p) {
     constexpr int VEC = 16 / sizeof(T);
+    const int lane = threadIdx.x & 31;
     const uint32_t nvec = (uint32_t)(p.n / VEC);
-    uint32_t v = blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t step = gridDim.x * blockDim.x;
-    for (; v < nvec; v += step) {
-        uint32_t o = fdiv(v, p.inner_v);
-        uint32_t w = v - o * p.inner_v.div;  // vector index inside the group
-        int64_t boff = outer_base(p, o);
-        float x[VEC], y[VEC];
-        if constexpr (sizeof(T) == 4) {
-            float4 a4 = ld_stream(reinterpret_cast<const float4*>(full) + v);
-            x[0] = a4.x; x[1] = a4.y; x[2] = a4.z; x[3] = a4.w;
-        } else {
-            unpack8(ld_stream(reinterpret_cast<const uint4*>(full) + v), x);
-        }
-        if (p.mode == 0) {
-            uint32_t c = w - fdiv(w, p.cc_v) * p.cc_v.div;
-            const T* bp = bc + boff + (int64_t)c * VEC;
-            if constexpr (sizeof(T) == 4) {
-                float4 b4 = __ldg(reinterpret_cast<const float4*>(bp));
-                y[0] = b4.x; y[1] = b4.y; y[2] = b4.z; y[3] = b4.w;
-            } else {
-                unpack8(__ldg(reinterpret_cast<const uint4*>(bp)), y);
-            }
-        } else {
-            float s = to_f(bc[boff]);
-#pragma unroll
-            for (int j = 0; j < VEC; ++j) y[j] = s;
-        }
-        float4* op = reinterpret_cast<float4*>(out) + (int64_t)v * (VEC / 4);
-#pragma unroll
-        for (int j = 0; j < VEC / 4; ++j)
-            st_stream(op + j, make_float4(x[4 * j] * y[4 * j], x[4 * j + 1] * y[4 * j + 1],
-                                          x[4 * j + 2] * y[4 * j + 2], x[4 * j + 3] * y[4 * j + 3]));
+    const uint4* src = reinterpret_cast<const uint4*>(full);
+    for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 2 * step) {
+        const uint32_t v1 = v + step;
+        const uint4 a0 = ld_stream(src + v);
+        uint4 a1 = make_uint4(0, 0, 0, 0);
+        if (v1 < nvec) a1 = ld_stream(src + v1);
+        bcast_apply<T>(bc, out, p, v, a0, lane, (int64_t)v - lane + 32 <= (int64_t)nvec);
+        if (v1 < nvec) bcast_apply<T>(bc, out, p, v1, a1, lane, (int64_t)v1 - lane + 32 <= (int64_t)nvec);
     }
 }
 
@@ -184,8 +257,8 @@ int elementwise_mul(int32_t dtype, const void* a, const void* b, float* out, int
             ew_mul_f32_vec<<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>(
                 (const float4*)a, (const float4*)b, (float4*)out, nvec);
         else
-            ew_mul_f16_vec<<<grid_for(nvec, 256), 256, 0, s>>>((const uint4*)a, (const uint4*)b,
-                                                               (float4*)out, nvec);
+            ew_mul_f16_vec<<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const uint4*)a, (const uint4*)b,
+                                                                         out, nvec);
         count_launch();
     }
     int64_t done = nvec * vec;
@@ -233,10 +306,10 @@ int broadcast_mul(const pe_broadcast_plan* pl, const void* full, const void* bc,
         }
         int64_t nvec = pl->n / vec;
         if (pl->dtype == PE_F32)
-            bcast_mul_vec<float><<<grid_for(nvec, 256), 256, 0, s>>>((const float*)full,
+            bcast_mul_vec<float><<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const float*)full,
                                                                     (const float*)bc, out, p);
         else
-            bcast_mul_vec<__half><<<grid_for(nvec, 256), 256, 0, s>>>((const __half*)full,
+            bcast_mul_vec<__half><<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const __half*)full,
                                                                      (const __half*)bc, out, p);
     } else {
         BcastGeneric p{};
