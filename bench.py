@@ -236,8 +236,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--shrink", type=int, default=1,
+                    help="divide the config's leading axis (small cases for profiler captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.shrink > 1:
+        eq, s0, s1, dt = CFG[args.config]
+        a0, b0 = eq.split("->")[0].split(",")
+        lead = eq.split("->")[1][0]
+        s0 = tuple(d // args.shrink if a0[i] == lead else d for i, d in enumerate(s0))
+        s1 = tuple(d // args.shrink if b0[i] == lead else d for i, d in enumerate(s1))
+        CFG[args.config] = (eq, s0, s1, dt)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

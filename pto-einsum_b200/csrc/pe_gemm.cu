@@ -81,7 +81,7 @@ struct Cfg {
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
     // epilogue warps (two per TMEM lane quadrant for fp16), 2 x 4 KB staging each
     static constexpr int EPIW = F32 ? 4 : 8;
-    static constexpr int EBUF = EPIW == 8 ? 1 : 2;   // 4 KB staging buffers per epilogue warp
+    static constexpr int EBUF = 1;   // one 4 KB transpose buffer per epilogue warp
     static constexpr int EPI_BYTES = EPIW * EBUF * 4096;
     static constexpr int STAGES = (224 * 1024 - EPI_BYTES) / STAGE_BYTES;
     static constexpr int UMMA_K = F32 ? 8 : 16;
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int ew = warp - 2;
         const int q = warp & 3;
         const int half = ew >> 2;
-        int acc = 0, buf = 0;
+        int acc = 0;
         uint32_t acc_phase = 0;
         uint8_t* stage_buf = epi + ew * C::EBUF * 4096;
         for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
@@ -320,51 +320,63 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             int cc[3];
             batch_coords(g.cb, bidx, cc);
             int64_t row_off = 0;
-            if (!g.out_tma && m < g.M) row_off = decode_off(g.ob, bidx) + decode_off(g.om, m);
-            uint32_t v[32], vn[32];
-            if (half < nvalid) {
-                __syncwarp();
-                tmem_ld32(tbase + half * 32, v);
-                tmem_ld_wait();
-            }
-#pragma unroll 1
-            for (int c = half; c < nvalid; c += NH) {
+            if (m < g.M) row_off = decode_off(g.ob, bidx) + decode_off(g.om, m);
+            // unit-stride outputs: row offsets are affine in the row index
+            const int64_t row_base = decode_off(g.ob, bidx);
+            const int64_t mst = g.om.stride[0];
+            // Sum the accumulator slots (fp32) and write one 32x32 chunk held as
+            // lane = row, v[j] = column nc + j.
+            auto emit = [&](uint32_t (&v)[32], int c) {
                 const int nc = n0 + c * 32;
-                const bool more = c + NH < nvalid;
-                __syncwarp();  // tcgen05.ld / wait::ld are .sync.aligned
                 if constexpr (C::F32) {
                     for (int sl = 1; sl < nslots; ++sl) {
                         uint32_t w[32];
+                        __syncwarp();
                         tmem_ld32(tbase + (uint32_t)(sl * C::BN) + c * 32, w);
                         tmem_ld_wait();
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
                             v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
                     }
-                    if (more) tmem_ld32(tbase + (c + NH) * 32, vn);
-                } else {
-                    if (more) tmem_ld32(tbase + (c + NH) * 32, vn);
                 }
                 if (g.out_tma) {
-                    uint8_t* sbuf = stage_buf + buf * 4096;
-                    if (lane == 0) {
-                        if constexpr (C::EBUF == 2) bulk_wait_read<1>();
-                        else bulk_wait_read<0>();
-                    }
-                    __syncwarp();
-                    uint8_t* row = sbuf + lane * 128;
+                    // Transpose the chunk through a 128B-swizzled staging buffer;
+                    // each store instruction then writes four 128-byte row pieces.
+                    // Global stores need no completion wait, so the buffer is free
+                    // again once read back.
+                    uint8_t* row = stage_buf + lane * 128;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         uint4 w = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                         *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = w;
                     }
-                    fence_proxy_async_smem();
                     __syncwarp();
-                    if (lane == 0 && mrow < g.M) {
-                        tma_store_5d(&g.tmc, smem_u32(sbuf), nc, mrow, cc[0], cc[1], cc[2]);
-                        bulk_commit();
+                    const int jj = lane & 7;
+                    const int n = nc + jj * 4;
+                    uint4 w[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const int rr = k * 4 + (lane >> 3);
+                        w[k] = *reinterpret_cast<const uint4*>(stage_buf + rr * 128 + ((jj ^ (rr & 7)) << 4));
                     }
-                    if constexpr (C::EBUF == 2) buf ^= 1;
+                    __syncwarp();
+                    {
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const int r = mrow + k * 4 + (lane >> 3);
+                            if (r < g.M) {
+                                float* dst = g.out + row_base + (int64_t)r * mst + n;
+                                if (n + 4 <= g.N) {
+                                    *reinterpret_cast<uint4*>(dst) = w[k];
+                                } else {
+                                    const uint32_t e4[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e)
+                                        if (n + e < g.N) dst[e] = __uint_as_float(e4[e]);
+                                }
+                            }
+                        }
+                    }
                 } else if (m < g.M) {
                     float* o = g.out + row_off;
 #pragma unroll
@@ -373,12 +385,28 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         if (n < g.N) o[decode_off(g.on, n)] = __uint_as_float(v[j]);
                     }
                 }
-                if (more) {
-                    __syncwarp();
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = vn[j];
-                }
+            };
+            // Two register buffers: the TMEM load of the next chunk is in flight
+            // while the current one is written out.
+            uint32_t va[32], vb[32];
+            if (half < nvalid) {
+                __syncwarp();
+                tmem_ld32(tbase + half * 32, va);
+                tmem_ld_wait();
+            }
+#pragma unroll 1
+            for (int c = half; c < nvalid; c += 2 * NH) {
+                const int c1 = c + NH, c2 = c + 2 * NH;
+                __syncwarp();
+                if (c1 < nvalid) tmem_ld32(tbase + c1 * 32, vb);
+                emit(va, c);
+                if (c1 >= nvalid) break;
+                __syncwarp();
+                tmem_ld_wait();
+                if (c2 < nvalid) tmem_ld32(tbase + c2 * 32, va);
+                emit(vb, c1);
+                __syncwarp();
+                if (c2 < nvalid) tmem_ld_wait();
             }
             tc_fence_before();
             __syncwarp();
@@ -388,7 +416,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 acc_phase ^= 1;
             }
         }
-        if (lane == 0) bulk_wait<0>();
     } else if constexpr (C::F32) {
         // ---------------- 3xTF32 split: x -> big (in place) + small ----------------
         const int st = threadIdx.x - 32 * (2 + C::EPIW);
