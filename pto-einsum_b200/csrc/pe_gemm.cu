@@ -67,7 +67,7 @@ struct GemmArgs {
     Decode ob, om, on;
 };
 
-template <int BN_, bool F32_>
+template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8)>
 struct Cfg {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
@@ -80,7 +80,10 @@ struct Cfg {
     static constexpr int TX_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
     // epilogue warps (two per TMEM lane quadrant for fp16), 2 x 4 KB staging each
-    static constexpr int EPIW = F32 ? 4 : 8;
+    // epilogue warps: 4 (one per TMEM lane quadrant) or more, sharing quadrants
+    // by alternating 32-column chunks; more warps raise the output rate of
+    // store-bound shapes, fewer leave shared memory for pipeline stages
+    static constexpr int EPIW = EPIW_;
     static constexpr int EBUF = 1;   // one 4 KB transpose buffer per epilogue warp
     static constexpr int EPI_BYTES = EPIW * EBUF * 4096;
     static constexpr int STAGES = (224 * 1024 - EPI_BYTES) / STAGE_BYTES;
