@@ -67,16 +67,21 @@ struct GemmArgs {
     Decode ob, om, on;
 };
 
-template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8)>
+template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8), bool PAIR_ = false>
 struct Cfg {
-    static constexpr int BM = 128;
+    // PAIR: a cluster of two CTAs computes one TM = 256-row tile with
+    // tcgen05 cta_group::2; each CTA lands 128 rows of A and half of B's N.
+    static constexpr bool PAIR = PAIR_;
+    static constexpr int BM = 128;                      // rows of A per CTA
+    static constexpr int TM = PAIR ? 256 : 128;         // rows of the output tile
     static constexpr int BN = BN_;
     static constexpr bool F32 = F32_;
     static constexpr int ES = F32 ? 4 : 2;
     static constexpr int BK = 128 / ES;                 // one 128-byte swizzle row
     static constexpr int MNBOX = 128 / ES;              // MN-major box width
     static constexpr int A_BYTES = BM * 128;
-    static constexpr int B_BYTES = BN * 128;
+    static constexpr int BNL = PAIR ? BN / 2 : BN;     // B columns landed per CTA
+    static constexpr int B_BYTES = BNL * 128;
     static constexpr int TX_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
     // epilogue warps (two per TMEM lane quadrant for fp16), 2 x 4 KB staging each
@@ -102,6 +107,7 @@ struct Cfg {
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+    static_assert(!PAIR || !F32, "CTA pairs are fp16-only");
 };
 
 // Batch coordinates of flat batch index i in one map (fully unrolled so the
@@ -153,6 +159,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     const int NBUF = C::SLOTS / S;              // accumulator buffers
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = C::PAIR ? cluster_rank() : 0;        // CTA rank in the pair
+    const int unit0 = C::PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int ustep = C::PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(full(s), 1);
@@ -161,7 +170,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         }
         for (int a = 0; a < 4; ++a) {
             mbar_init(tfull(a), 1);
-            mbar_init(tempty(a), C::EPIW);
+            mbar_init(tempty(a), C::PAIR ? 2 * C::EPIW : C::EPIW);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
@@ -171,11 +180,17 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         if (g.out_tma) tma_prefetch(&g.tmc);
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (C::PAIR) {
+            tmem_alloc_pair(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+            tmem_relinquish();
+        }
         tc_fence_before();
     }
     __syncthreads();
+    if constexpr (C::PAIR) cluster_sync();  // barrier inits visible to the peer CTA
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int per_batch = g.mblk * g.nblk;
@@ -186,11 +201,12 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_par = 0;
-            for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+            for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
                 const int t = u / g.ksplit, sp = u - t * g.ksplit;
                 const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
                 const int i = t / per_batch, r = t - i * per_batch;
-                const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
+                const int m0 = (r / g.nblk) * C::TM + (int)rank * C::BM;   // this CTA's A rows
+                const int n0 = (r % g.nblk) * C::BN + (int)rank * (C::BN - C::BNL);  // its B columns
                 int ca[3], cb[3];
                 batch_coords(g.ab, i, ca);
                 batch_coords(g.bb, i, cb);
@@ -199,24 +215,29 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     uint8_t* sb = sa + C::A_BYTES;
                     const int k0 = kb * C::BK;
-                    mbar_arrive_expect_tx(full(stage), C::TX_BYTES);
+                    // pairs: the leader's barrier counts both CTAs' bytes
+                    if (rank == 0) mbar_arrive_expect_tx(full(stage), C::TX_BYTES * (C::PAIR ? 2 : 1));
                     issued_mask |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+                    auto load = [&](uint32_t dst, const CUtensorMap* tm, int x0, int x1, const int (&c)[3]) {
+                        if constexpr (C::PAIR)
+                            tma_load_5d_pair(dst, tm, full(stage), x0, x1, c[0], c[1], c[2]);
+                        else
+                            tma_load_5d(dst, tm, full(stage), x0, x1, c[0], c[1], c[2]);
+                    };
                     if (!g.a_mn) {
-                        tma_load_5d(smem_u32(sa), &g.tma, full(stage), k0, m0, ca[0], ca[1], ca[2]);
+                        load(smem_u32(sa), &g.tma, k0, m0, ca);
                     } else {
 #pragma unroll
                         for (int j = 0; j < C::BM / C::MNBOX; ++j)
-                            tma_load_5d(smem_u32(sa + j * C::BK * 128), &g.tma, full(stage),
-                                        m0 + j * C::MNBOX, k0, ca[0], ca[1], ca[2]);
+                            load(smem_u32(sa + j * C::BK * 128), &g.tma, m0 + j * C::MNBOX, k0, ca);
                     }
                     if (!g.b_mn) {
-                        tma_load_5d(smem_u32(sb), &g.tmb, full(stage), k0, n0, cb[0], cb[1], cb[2]);
+                        load(smem_u32(sb), &g.tmb, k0, n0, cb);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < C::BN / C::MNBOX; ++j)
-                            tma_load_5d(smem_u32(sb + j * C::BK * 128), &g.tmb, full(stage),
-                                        n0 + j * C::MNBOX, k0, cb[0], cb[1], cb[2]);
+                        for (int j = 0; j < C::BNL / C::MNBOX; ++j)
+                            load(smem_u32(sb + j * C::BK * 128), &g.tmb, n0 + j * C::MNBOX, k0, cb);
                     }
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -224,16 +245,17 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     }
                 }
             }
-            if (*abort_flag) {
+            if (*abort_flag && rank == 0) {
                 // let every load still in flight land before shared memory is released
+                // (pairs: the leader's barriers also count the peer's loads)
                 for (int s = 0; s < C::STAGES; ++s)
                     if (issued_mask & (1u << s)) drain_wait(full(s), (issued_par >> s) & 1);
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // ---------------- MMA issuer ----------------
-            const uint32_t idesc = make_idesc(C::F32 ? 2u : 0u, C::BM, C::BN, g.a_mn, g.b_mn);
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (pairs: the leader CTA only) ----------------
+            const uint32_t idesc = make_idesc(C::F32 ? 2u : 0u, C::TM, C::BN, g.a_mn, g.b_mn);
             // byte step of one UMMA_K slice and leading offsets of MN-major tiles
             const uint32_t a_kstep = g.a_mn ? (C::UMMA_K / 8) * 1024 : 32;
             const uint32_t b_kstep = g.b_mn ? (C::UMMA_K / 8) * 1024 : 32;
@@ -245,7 +267,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const uint32_t a_sbo = a_lay == 1 ? 512 : 1024, b_sbo = b_lay == 1 ? 512 : 1024;
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+            for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
                 const int t = u / g.ksplit, sp = u - t * g.ksplit;
                 const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
                 if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
@@ -273,25 +295,30 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                             mma_tf32(d, ads, bd, idesc, accum);
                             mma_tf32(d, ad, bds, idesc, 1u);
                             mma_tf32(d, ad, bd, idesc, 1u);
+                        } else if constexpr (C::PAIR) {
+                            mma_f16_pair(d, ad, bd, idesc, accum);
                         } else {
                             mma_f16(d, ad, bd, idesc, accum);
                         }
                     }
-                    mma_commit(empty(stage));
+                    if constexpr (C::PAIR) mma_commit_pair_mc(empty(stage), 0x3);
+                    else mma_commit(empty(stage));
                     if (++stage == C::STAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
                 }
                 if (!ok) break;
-                mma_commit(tfull(acc));
+                if constexpr (C::PAIR) mma_commit_pair_mc(tfull(acc), 0x3);
+                else mma_commit(tfull(acc));
                 if (++acc == NBUF) {
                     acc = 0;
                     acc_phase ^= 1;
                 }
             }
             // all MMAs issued by this thread complete before TMEM is released
-            mma_commit(mma_done);
+            if constexpr (C::PAIR) mma_commit_pair(mma_done);
+            else mma_commit(mma_done);
             drain_wait(mma_done, 0);
         }
     } else if (warp < 2 + C::EPIW) {
@@ -307,11 +334,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         int acc = 0;
         uint32_t acc_phase = 0;
         uint8_t* stage_buf = epi + ew * C::EBUF * 4096;
-        for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+        for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
             const int t = u / g.ksplit, sp = u - t * g.ksplit;
             const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             const int i = t / per_batch, r = t - i * per_batch;
-            const int m0 = (r / g.nblk) * C::BM, n0 = (r % g.nblk) * C::BN;
+            const int m0 = (r / g.nblk) * C::TM + (int)rank * C::BM, n0 = (r % g.nblk) * C::BN;
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
             tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * S * C::BN);
@@ -413,7 +440,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(tempty(acc));
+            if (lane == 0) {
+                if constexpr (C::PAIR) mbar_arrive_cluster(map_to_rank(tempty(acc), 0));  // leader's barrier
+                else mbar_arrive(tempty(acc));
+            }
             if (++acc == NBUF) {
                 acc = 0;
                 acc_phase ^= 1;
@@ -424,7 +454,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int st = threadIdx.x - 32 * (2 + C::EPIW);
         int stage = 0;
         uint32_t phase = 0;
-        for (int u = blockIdx.x; u < g.tiles * g.ksplit && !*abort_flag; u += gridDim.x) {
+        for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
                 const int t = u / g.ksplit, sp = u - t * g.ksplit;
                 const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             bool ok = true;
@@ -459,10 +489,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     }
 
     __syncthreads();
+    // pairs: the leader's MMAs write the peer's TMEM and both CTAs' barriers
+    // receive remote arrivals, so neither CTA leaves before the other is done
+    if constexpr (C::PAIR) cluster_sync();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        if constexpr (C::PAIR) tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+        else tmem_dealloc(tmem_base, C::TMEM_COLS);
     }
 }
 
@@ -689,7 +723,7 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
             done[dev] = true;
         }
     }
-    g.mblk = (int)((g.M + C::BM - 1) / C::BM);
+    g.mblk = (int)((g.M + C::TM - 1) / C::TM);
     g.nblk = (int)((g.N + C::BN - 1) / C::BN);
     g.kiters = (int)((g.K + C::BK - 1) / C::BK);
     if (g.ksplit <= 1 || g.kiters < 2) {
@@ -702,6 +736,25 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
     int64_t tiles = (int64_t)g.mblk * g.nblk * (int64_t)g.tiles;  // g.tiles holds I on entry
     if (tiles > 0x7FFFFFFF) return set_last_error(PE_ERR_UNSUPPORTED);
     g.tiles = (int)tiles;
+    if constexpr (C::PAIR) {
+        // one cluster of two CTAs per tile pair, persistent over the SMs
+        const int pairs = (int)std::min<int64_t>(tiles * g.ksplit, num_sms() / 2);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<C>, g);
+        count_launch();
+        return check_cuda(e);
+    }
     int grid = std::min<int64_t>(tiles * g.ksplit, num_sms());
     gemm_kernel<C><<<grid, C::THREADS, C::SMEM, s>>>(g);
     count_launch();
@@ -713,6 +766,13 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
 // TMA-landed x already acts as "big" and only "small" = x - big needs writing.
 // PE_TF32_HW_TRUNC=0 restores the explicit masked write-back; a GPU test pins
 // that both give bit-identical results.
+// fp16 wide tiles run as CTA pairs (tcgen05 cta_group::2, 256x256 tiles)
+// unless PE_GEMM_PAIRS=0.
+int pairs_enabled() {
+    const char* e = getenv("PE_GEMM_PAIRS");
+    return (e && e[0] == '0') ? 0 : 1;
+}
+
 int raw_big_enabled() {
     const char* e = getenv("PE_TF32_HW_TRUNC");
     return (e && e[0] == '0') ? 0 : 1;
@@ -1039,9 +1099,15 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
             return set_last_error(PE_ERR_UNSUPPORTED);
         rc = launch_gemm<Cfg<128, true>>(g, s);
     } else {
-        if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, L.bn))
+        // pairs halve each SM's operand traffic, which pays off where the
+        // mainloop dominates (long K); output-bound short-K shapes stay single
+        const bool pair = L.bn == 256 && g.K >= 512 && pairs_enabled();
+        if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, pair ? 128 : L.bn))
             return set_last_error(PE_ERR_UNSUPPORTED);
-        rc = L.bn == 256 ? launch_gemm<Cfg<256, false>>(g, s) : launch_gemm<Cfg<128, false>>(g, s);
+        if (pair)
+            rc = launch_gemm<Cfg<256, false, 8, true>>(g, s);
+        else
+            rc = L.bn == 256 ? launch_gemm<Cfg<256, false>>(g, s) : launch_gemm<Cfg<128, false>>(g, s);
     }
     if (rc || L.ksplit <= 1) return rc;
     return splitk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g.ksplit, s);

@@ -245,3 +245,29 @@ def test_validation_errors_cuda():
         run(a, b.half())
     with pytest.raises(ValueError, match="same CUDA device"):
         run(a.cpu(), b.cpu())
+
+
+PAIR_CASES = [  # fp16 shapes with >= 148 wide (256-column) tiles: the CTA-pair kernel
+    ("bij, bjk -> bik", (40, 512, 512), (40, 512, 512)),     # B MN-major
+    ("bij, bjk -> bik", (40, 300, 136), (40, 136, 520)),     # partial M and N tiles, K not a tile multiple
+    ("bshd, bthd -> bsht", (4, 512, 8, 512), (4, 512, 8, 512)),  # B K-major, permuted output
+    ("bik, bjk -> bij", (24, 384, 256), (24, 768, 256)),     # K-major both
+]
+
+
+@pytest.mark.parametrize("eq,s0,s1", PAIR_CASES, ids=[case_id(*c) for c in PAIR_CASES])
+def test_cta_pair_kernel(eq, s0, s1, monkeypatch):
+    """tcgen05 cta_group::2 tiles (two CTAs per 256x256 tile) against the oracle
+    and against the single-CTA kernel."""
+    a, b = seeded(s0, torch.float16, 51, "randn"), seeded(s1, torch.float16, 52, "randn")
+    ref = oracle.einsum_cpu(eq, a, b)
+    monkeypatch.setenv("PE_GEMM_PAIRS", "1")
+    pair = einsum(eq, a.cuda(), b.cuda())
+    check_close(pair, ref, torch.float16)
+    for _ in range(3):
+        assert torch.equal(einsum(eq, a.cuda(), b.cuda()), pair)
+    monkeypatch.setenv("PE_GEMM_PAIRS", "0")
+    single = einsum(eq, a.cuda(), b.cuda())
+    check_close(single, ref, torch.float16)
+    torch.testing.assert_close(pair, single, rtol=1e-5, atol=1e-5)
+    assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
