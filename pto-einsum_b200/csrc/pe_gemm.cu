@@ -53,6 +53,9 @@ struct GemmArgs {
     CUtensorMap tma;
     CUtensorMap tmb;
     CUtensorMap tmc;
+    CUtensorMap tmas;   // fp32: precomputed tf32 "small" halves of A / B (same layout)
+    CUtensorMap tmbs;
+    int a_pre, b_pre;   // fp32: operand's small half comes from tmas / tmbs
     int M, N, K;
     int mblk, nblk, tiles, kiters;
     int a_mn, b_mn;
@@ -67,7 +70,7 @@ struct GemmArgs {
     Decode ob, om, on;
 };
 
-template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8), bool PAIR_ = false>
+template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8), bool PAIR_ = false, int SPLITW_ = (F32_ ? 4 : 0)>
 struct Cfg {
     // PAIR: a cluster of two CTAs computes one TM = 256-row tile with
     // tcgen05 cta_group::2; each CTA lands 128 rows of A and half of B's N.
@@ -102,7 +105,10 @@ struct Cfg {
     // 4 / S buffers alternate between tiles.
     static constexpr int SLOTS = F32 ? 4 : 2;
     static constexpr int TMEM_COLS = SLOTS * BN;
-    static constexpr int THREADS = 64 + 32 * EPIW + (F32 ? 128 : 0);
+    // fp32: warps computing the tf32 small halves in shared memory (0 when
+    // the variant is only used with both halves precomputed)
+    static constexpr int SPLITW = SPLITW_;
+    static constexpr int THREADS = 64 + 32 * EPIW + 32 * SPLITW;
     static constexpr int NBARS = 3 * STAGES + 9;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
     static_assert(SMEM <= 232448, "shared memory budget");
@@ -156,6 +162,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     auto tempty = [&](int a) { return bar0 + 8u * (3 * C::STAGES + 4 + a); };
     const uint32_t mma_done = bar0 + 8u * (3 * C::STAGES + 8);
     const int S = C::F32 ? g.acc_slots : 1;     // accumulator slots per tile
+    const bool split_done_by_tma = g.a_pre && g.b_pre;  // fp32: both small halves precomputed
     const int NBUF = C::SLOTS / S;              // accumulator buffers
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -216,7 +223,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     uint8_t* sb = sa + C::A_BYTES;
                     const int k0 = kb * C::BK;
                     // pairs: the leader's barrier counts both CTAs' bytes
-                    if (rank == 0) mbar_arrive_expect_tx(full(stage), C::TX_BYTES * (C::PAIR ? 2 : 1));
+                    int tx = C::TX_BYTES * (C::PAIR ? 2 : 1);
+                    if constexpr (C::F32) tx += (g.a_pre ? C::A_BYTES : 0) + (g.b_pre ? C::B_BYTES : 0);
+                    if (rank == 0) mbar_arrive_expect_tx(full(stage), tx);
                     issued_mask |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
                     auto load = [&](uint32_t dst, const CUtensorMap* tm, int x0, int x1, const int (&c)[3]) {
@@ -225,19 +234,29 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         else
                             tma_load_5d(dst, tm, full(stage), x0, x1, c[0], c[1], c[2]);
                     };
-                    if (!g.a_mn) {
-                        load(smem_u32(sa), &g.tma, k0, m0, ca);
-                    } else {
+                    auto load_a = [&](uint8_t* dst, const CUtensorMap* tm) {
+                        if (!g.a_mn) {
+                            load(smem_u32(dst), tm, k0, m0, ca);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < C::BM / C::MNBOX; ++j)
-                            load(smem_u32(sa + j * C::BK * 128), &g.tma, m0 + j * C::MNBOX, k0, ca);
-                    }
-                    if (!g.b_mn) {
-                        load(smem_u32(sb), &g.tmb, k0, n0, cb);
-                    } else {
+                            for (int j = 0; j < C::BM / C::MNBOX; ++j)
+                                load(smem_u32(dst + j * C::BK * 128), tm, m0 + j * C::MNBOX, k0, ca);
+                        }
+                    };
+                    auto load_b = [&](uint8_t* dst, const CUtensorMap* tm) {
+                        if (!g.b_mn) {
+                            load(smem_u32(dst), tm, k0, n0, cb);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < C::BNL / C::MNBOX; ++j)
-                            load(smem_u32(sb + j * C::BK * 128), &g.tmb, n0 + j * C::MNBOX, k0, cb);
+                            for (int j = 0; j < C::BNL / C::MNBOX; ++j)
+                                load(smem_u32(dst + j * C::BK * 128), tm, n0 + j * C::MNBOX, k0, cb);
+                        }
+                    };
+                    load_a(sa, &g.tma);
+                    load_b(sb, &g.tmb);
+                    if constexpr (C::F32) {
+                        if (g.a_pre) load_a(sa + C::TX_BYTES, &g.tmas);
+                        if (g.b_pre) load_b(sb + C::TX_BYTES, &g.tmbs);
                     }
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -275,7 +294,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 const uint32_t dbuf = tmem_base + (uint32_t)(acc * S * C::BN);
                 bool ok = true;
                 for (int kb = kb_lo; kb < kb_hi; ++kb) {
-                    if (!mbar_wait(C::F32 ? split(stage) : full(stage), phase, abort_flag, 3)) {
+                    if (!mbar_wait(C::F32 && !split_done_by_tma ? split(stage) : full(stage), phase, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
@@ -449,12 +468,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 acc_phase ^= 1;
             }
         }
-    } else if constexpr (C::F32) {
+    } else if constexpr (C::F32 && C::SPLITW == 4) {
         // ---------------- 3xTF32 split: x -> big (in place) + small ----------------
         const int st = threadIdx.x - 32 * (2 + C::EPIW);
+        // 16-byte pieces to split this stage: operands whose small half was
+        // precomputed arrive with it and are skipped
+        const int jlo = g.a_pre ? C::A_BYTES / 16 : 0;
+        const int jhi = g.b_pre ? C::A_BYTES / 16 : C::TX_BYTES / 16;
         int stage = 0;
         uint32_t phase = 0;
-        for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
+        for (int u = split_done_by_tma ? g.tiles * g.ksplit : unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
                 const int t = u / g.ksplit, sp = u - t * g.ksplit;
                 const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
             bool ok = true;
@@ -466,7 +489,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 uint4* big = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
                 uint4* small = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES + C::TX_BYTES);
 #pragma unroll 4
-                for (int j = st; j < C::TX_BYTES / 16; j += 128) {
+                for (int j = jlo + st; j < jhi; j += 128) {
                     uint4 x = big[j];
                     uint4 h = make_uint4(x.x & 0xFFFFE000u, x.y & 0xFFFFE000u, x.z & 0xFFFFE000u,
                                          x.w & 0xFFFFE000u);
@@ -778,6 +801,31 @@ int raw_big_enabled() {
     return (e && e[0] == '0') ? 0 : 1;
 }
 
+// tf32 "small" half of fp32 data: y = x - (x with its low 13 mantissa bits
+// cleared). x - trunc(x) is exact in fp32.
+__global__ void __launch_bounds__(256) tf32_small(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t v = i; v < n4; v += step) {
+        const float4 a = reinterpret_cast<const float4*>(x)[v];
+        float4 r;
+        r.x = a.x - __uint_as_float(__float_as_uint(a.x) & 0xFFFFE000u);
+        r.y = a.y - __uint_as_float(__float_as_uint(a.y) & 0xFFFFE000u);
+        r.z = a.z - __uint_as_float(__float_as_uint(a.z) & 0xFFFFE000u);
+        r.w = a.w - __uint_as_float(__float_as_uint(a.w) & 0xFFFFE000u);
+        reinterpret_cast<float4*>(y)[v] = r;
+    }
+    for (int64_t e = 4 * n4 + i; e < n; e += step) y[e] = x[e] - __uint_as_float(__float_as_uint(x[e]) & 0xFFFFE000u);
+}
+
+int tf32_small_launch(const void* x, void* y, int64_t n, cudaStream_t s) {
+    int64_t blocks = (n / 4 + 255) / 256 + 1, cap = (int64_t)num_sms() * 8;
+    tf32_small<<<(int)std::min(blocks, cap), 256, 0, s>>>((const float*)x, (float*)y, n);
+    count_launch();
+    return check_cuda(cudaGetLastError());
+}
+
 // Split-K reduction: out[perm(e)] = sum over sp of part[sp][e] (fixed order,
 // so results are run-to-run identical). e walks the canonical [I, L0, L1]
 // index; `od` decodes it into the permuted output offset.
@@ -801,6 +849,10 @@ struct Lowered {
     bool a_ws = false, b_ws = false;
     int64_t kpad = 0;             // padded row length of workspace operands
     size_t a_off = 0, b_off = 0, p_off = 0, ws_bytes = 0;
+    // fp32: precomputed tf32 "small" halves (same layout as the raw operand)
+    bool a_pre = false, b_pre = false;
+    size_t as_off = 0, bs_off = 0;
+    int64_t n_in0 = 0, n_in1 = 0;        // raw operand element counts
     int bn = 128;                 // N tile of the chosen kernel
     int ksplit = 1;               // split-K factor (partials in the workspace when > 1)
     // group axes
@@ -926,6 +978,27 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
                 best = cost;
                 L->ksplit = ks;
             }
+        }
+    }
+    // fp32 operands that are small next to the output get their tf32 small
+    // halves computed once by a streaming pass instead of by the split warps
+    // for every tile that reads them (4a: 4 MB operands, 268 MB output).
+    if (es == 4) {
+        int64_t n0e = 1, n1e = 1;
+        for (int a = 0; a < pl->rank0; ++a) n0e *= pl->shape0[a];
+        for (int a = 0; a < pl->rank1; ++a) n1e *= pl->shape1[a];
+        L->n_in0 = n0e;
+        L->n_in1 = n1e;
+        const int64_t cap = (int64_t)16 << 20;  // elements (64 MB)
+        if (L->a.direct && n0e <= cap) {
+            L->a_pre = true;
+            L->as_off = off;
+            off += ((size_t)n0e * 4 + 255) & ~(size_t)255;
+        }
+        if (L->b.direct && n1e <= cap) {
+            L->b_pre = true;
+            L->bs_off = off;
+            off += ((size_t)n1e * 4 + 255) & ~(size_t)255;
         }
     }
     if (L->ksplit > 1) {
@@ -1095,9 +1168,29 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
         // more slots for long contractions: fewer accumulation steps per slot
         const int64_t kit = (pl->C + 31) / 32;
         g.acc_slots = kit >= 32 ? 4 : (kit >= 8 ? 2 : 1);
+        if (L.a_pre) {
+            void* sm = (uint8_t*)ws + L.as_off;
+            rc = tf32_small_launch(in0, sm, L.n_in0, s);
+            if (rc) return rc;
+            OperandView v = va;
+            v.base = sm;
+            if (!encode_operand(&g.tmas, v, true, 128)) return set_last_error(PE_ERR_UNSUPPORTED);
+            g.a_pre = 1;
+        }
+        if (L.b_pre) {
+            void* sm = (uint8_t*)ws + L.bs_off;
+            rc = tf32_small_launch(in1, sm, L.n_in1, s);
+            if (rc) return rc;
+            OperandView v = vb;
+            v.base = sm;
+            if (!encode_operand(&g.tmbs, v, true, 128)) return set_last_error(PE_ERR_UNSUPPORTED);
+            g.b_pre = 1;
+        }
         if (!encode_operand(&g.tma, va, true, 128) || !encode_operand(&g.tmb, vb, true, 128))
             return set_last_error(PE_ERR_UNSUPPORTED);
-        rc = launch_gemm<Cfg<128, true>>(g, s);
+        // both small halves precomputed: the split warps have nothing to do, so
+        // spend the threads on epilogue warps instead (output-bound shapes)
+        rc = (g.a_pre && g.b_pre) ? launch_gemm<Cfg<128, true, 8, false, 0>>(g, s) : launch_gemm<Cfg<128, true>>(g, s);
     } else {
         // pairs halve each SM's operand traffic, which pays off where the
         // mainloop dominates (long K); output-bound short-K shapes stay single
