@@ -227,6 +227,64 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line))
 
 
+def _time(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_callers_suite(args):
+    """SURVEY 8(f) chained callers: the reference's LLM contraction patterns and the
+    linear-attention chain (bench_linear_attention.py), B200 vs torch.einsum."""
+    from llm_patterns import LARGE, PATTERNS, shapes
+    from pto_einsum import EinsumBuilder
+    from oracle.oracle import rel_frobenius
+    dev = torch.device("cuda", 0)
+    steps, warmup = max(args.steps // 10, 5), args.warmup
+    for dt in (torch.float16, torch.float32):
+        for name, eq in PATTERNS:
+            s0, s1 = shapes(eq, LARGE)
+            g = torch.Generator(device="cpu").manual_seed(7)
+            a = torch.randn(s0, generator=g).to(dt).to(dev)
+            b = torch.randn(s1, generator=g).to(dt).to(dev)
+            run = EinsumBuilder(eq, [s0, s1], dt).build()
+            ms = _time(lambda: run(a, b), steps, warmup)
+            mt = _time(lambda: torch.einsum(eq, a, b), steps, warmup)
+            err = rel_frobenius(run(a, b).cpu().numpy(), torch.einsum(eq, a.float(), b.float()).cpu().numpy())
+            print(json.dumps({"suite": "callers", "op": name, "equation": eq, "dtype": str(dt).split(".")[-1],
+                              "shape0": s0, "shape1": s1, "ms": round(ms, 4), "torch_ms": round(mt, 4),
+                              "speedup_vs_torch": round(mt / ms, 3), "rel_frobenius_vs_torch_fp32": err}))
+            del a, b, run
+            torch.cuda.empty_cache()
+        # linear-attention chain tn,sn,sp,ts->tp as three two-way einsums (config 4)
+        T, N, P = 8192, 128, 128
+        g = torch.Generator(device="cpu").manual_seed(8)
+        Q = torch.randn(T, N, generator=g).to(dt).to(dev)
+        K = torch.randn(T, N, generator=g).to(dt).to(dev)
+        V = torch.randn(T, P, generator=g).to(dt).to(dev)
+        t = torch.arange(T, dtype=torch.float32, device=dev)
+        D = torch.where(t[:, None] >= t[None, :], torch.pow(0.99, (t[:, None] - t[None, :]).clamp(min=0)),
+                        torch.zeros((), device=dev)).to(dt)
+        r1 = EinsumBuilder("tn,sn->ts", [(T, N), (T, N)], dt).build()
+        r2 = EinsumBuilder("ts,ts->ts", [(T, T), (T, T)], dt).build()
+        r3 = EinsumBuilder("ts,sp->tp", [(T, T), (T, P)], dt).build()
+        chain = lambda: r3(r2(r1(Q, K).to(dt), D).to(dt), V)  # noqa: E731
+        ms = _time(chain, steps, warmup)
+        mt = _time(lambda: torch.einsum("tn,sn,sp,ts->tp", Q, K, V, D), steps, warmup)
+        err = rel_frobenius(chain().cpu().numpy(),
+                            torch.einsum("tn,sn,sp,ts->tp", Q.float(), K.float(), V.float(), D.float()).cpu().numpy())
+        print(json.dumps({"suite": "callers", "op": "linear_attention_chain", "equation": "tn,sn,sp,ts->tp",
+                          "dtype": str(dt).split(".")[-1], "T": T, "ms": round(ms, 4), "torch_ms": round(mt, 4),
+                          "speedup_vs_torch": round(mt / ms, 3), "rel_frobenius_vs_torch_fp32": err}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -236,6 +294,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--suite", default=None, choices=["callers"],
+                    help="instead of the one-line benchmark: time the LLM contraction patterns and the "
+                         "linear-attention chain against torch.einsum (one JSON line per op)")
     ap.add_argument("--shrink", type=int, default=1,
                     help="divide the config's leading axis (small cases for profiler captures)")
     args = ap.parse_args()
@@ -253,6 +314,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
+        return
+    if args.suite == "callers":
+        run_callers_suite(args)
         return
 
     dist = None

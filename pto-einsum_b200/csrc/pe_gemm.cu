@@ -29,6 +29,8 @@
 #include <cstring>
 #include <mutex>
 
+#include <cuda_fp16.h>
+
 #include "pe_common.cuh"
 
 namespace pe {
@@ -801,6 +803,54 @@ int raw_big_enabled() {
     return (e && e[0] == '0') ? 0 : 1;
 }
 
+// Streaming contraction for degenerate shapes: one thread per output element
+// (output order, so stores coalesce); products and sums in fp32 in the
+// contraction order of the CPU reference, each rounded once, so fp32 results
+// match it bit for bit.
+struct SimtArgs {
+    int nd, nk;
+    FastDiv div[PE_MAX_RANK];                 // output axes (outermost first)
+    int64_t sa[PE_MAX_RANK], sb[PE_MAX_RANK]; // their strides in A and B
+    int64_t ksize[PE_MAX_RANK], ka[PE_MAX_RANK], kb[PE_MAX_RANK];  // contraction axes
+    int64_t n, C;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) small_contract(const T* __restrict__ A, const T* __restrict__ B,
+                                                      float* __restrict__ out, SimtArgs p) {
+    const uint32_t step = gridDim.x * blockDim.x;
+    for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < (uint32_t)p.n; e += step) {
+        uint32_t rem = e;
+        int64_t ao = 0, bo = 0;
+        for (int a = p.nd - 1; a >= 0; --a) {
+            const uint32_t q = fdiv(rem, p.div[a]);
+            const uint32_t idx = rem - q * p.div[a].div;
+            rem = q;
+            ao += (int64_t)idx * p.sa[a];
+            bo += (int64_t)idx * p.sb[a];
+        }
+        float acc = 0.f;
+        if (p.nk <= 1) {
+            const int64_t ka = p.nk ? p.ka[0] : 0, kb = p.nk ? p.kb[0] : 0;
+            for (int64_t c = 0; c < p.C; ++c)
+                acc = __fadd_rn(acc, __fmul_rn((float)A[ao + c * ka], (float)B[bo + c * kb]));
+        } else {
+            for (int64_t c = 0; c < p.C; ++c) {
+                int64_t r = c, oa = ao, ob = bo;
+                for (int a = p.nk - 1; a >= 0; --a) {
+                    const int64_t q = r / p.ksize[a];
+                    const int64_t idx = r - q * p.ksize[a];
+                    r = q;
+                    oa += idx * p.ka[a];
+                    ob += idx * p.kb[a];
+                }
+                acc = __fadd_rn(acc, __fmul_rn((float)A[oa], (float)B[ob]));
+            }
+        }
+        out[e] = acc;
+    }
+}
+
 // tf32 "small" half of fp32 data: y = x - (x with its low 13 mantissa bits
 // cleared). x - trunc(x) is exact in fp32.
 __global__ void __launch_bounds__(256) tf32_small(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
@@ -854,6 +904,7 @@ struct Lowered {
     size_t as_off = 0, bs_off = 0;
     int64_t n_in0 = 0, n_in1 = 0;        // raw operand element counts
     int bn = 128;                 // N tile of the chosen kernel
+    bool simt = false;            // degenerate shape: streaming kernel instead of the GEMM
     int ksplit = 1;               // split-K factor (partials in the workspace when > 1)
     // group axes
     Axis a_batch[PE_MAX_RANK], a_free[PE_MAX_RANK], a_ct[PE_MAX_RANK];
@@ -946,6 +997,16 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
     L->b_ws = !L->b.direct;
     const int64_t vec = 16 / es;
     L->kpad = ((C > 0 ? C : 1) + vec - 1) / vec * vec;
+    // Degenerate contractions (a free dim of at most 4 with a short
+    // contraction, e.g. a broadcast planned as 262144 batches of 4x1x1) would
+    // fill a 128-row MMA tile with almost nothing; they run on the streaming
+    // kernel and need no scratch.
+    L->simt = std::min(L0, L1) <= 4 && C <= 64;
+    if (L->simt) {
+        L->a_ws = L->b_ws = false;
+        L->ws_bytes = 0;
+        return PE_OK;
+    }
     size_t off = 0;
     if (L->a_ws) {
         L->a_off = off;
@@ -1046,6 +1107,59 @@ int splitk_reduce_launch(const float* part, float* out, const Lowered& L, const 
     return check_cuda(cudaGetLastError());
 }
 
+int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
+                          float* out, cudaStream_t s) {
+    // output axes in output order with their A / B strides
+    SimtArgs p{};
+    int64_t st0[PE_MAX_RANK], st1[PE_MAX_RANK], run = 1;
+    for (int a = pl->rank0 - 1; a >= 0; --a) { st0[a] = run; run *= pl->shape0[a]; }
+    run = 1;
+    for (int a = pl->rank1 - 1; a >= 0; --a) { st1[a] = run; run *= pl->shape1[a]; }
+    const int nb = L.nb, n0 = L.n0, n1 = L.n1;
+    // interp axis j -> (A stride, B stride)
+    int64_t ia[PE_MAX_RANK], ib[PE_MAX_RANK], isz[PE_MAX_RANK];
+    for (int j = 0; j < nb; ++j) { ia[j] = L.a_batch[j].stride; ib[j] = L.b_batch[j].stride; isz[j] = L.a_batch[j].size; }
+    for (int j = 0; j < n0; ++j) { ia[nb + j] = L.a_free[j].stride; ib[nb + j] = 0; isz[nb + j] = L.a_free[j].size; }
+    for (int j = 0; j < n1; ++j) { ia[nb + n0 + j] = 0; ib[nb + n0 + j] = L.b_free[j].stride; isz[nb + n0 + j] = L.b_free[j].size; }
+    int64_t n = 1;
+    for (int q = 0; q < pl->out_rank; ++q) {
+        const int j = pl->out_perm[q];
+        if (isz[j] == 1) continue;
+        p.div[p.nd] = make_fastdiv((uint32_t)isz[j]);
+        p.sa[p.nd] = ia[j];
+        p.sb[p.nd] = ib[j];
+        p.nd++;
+        n *= isz[j];
+    }
+    for (int j = 0; j < L.nc; ++j) {
+        if (L.a_ct[j].size == 1) continue;
+        if (p.nk > 0 && p.ka[p.nk - 1] == L.a_ct[j].stride * L.a_ct[j].size &&
+            p.kb[p.nk - 1] == L.b_ct[j].stride * L.b_ct[j].size) {
+            p.ksize[p.nk - 1] *= L.a_ct[j].size;
+            p.ka[p.nk - 1] = L.a_ct[j].stride;
+            p.kb[p.nk - 1] = L.b_ct[j].stride;
+        } else {
+            p.ksize[p.nk] = L.a_ct[j].size;
+            p.ka[p.nk] = L.a_ct[j].stride;
+            p.kb[p.nk] = L.b_ct[j].stride;
+            p.nk++;
+        }
+    }
+    p.n = n;
+    p.C = pl->C;
+    if (n >= (1ll << 32)) return set_last_error(PE_ERR_UNSUPPORTED);
+    (void)st0;
+    (void)st1;
+    int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms() * 8;
+    const int grid = (int)std::min(blocks, cap);
+    if (pl->dtype == PE_F32)
+        small_contract<float><<<grid, 256, 0, s>>>((const float*)in0, (const float*)in1, out, p);
+    else
+        small_contract<__half><<<grid, 256, 0, s>>>((const __half*)in0, (const __half*)in1, out, p);
+    count_launch();
+    return check_cuda(cudaGetLastError());
+}
+
 OperandView canonical_view(const void* base, int64_t I, int64_t L, int64_t C, int64_t kpad) {
     OperandView v;
     v.direct = true;
@@ -1096,6 +1210,7 @@ int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float
     if (!out) return set_last_error(PE_ERR_INVALID);
     if (pl->C == 0) return check_cuda(cudaMemsetAsync(out, 0, (size_t)n_out * 4, s));
     if (!in0 || !in1) return set_last_error(PE_ERR_INVALID);
+    if (L.simt) return small_contract_launch(pl, L, in0, in1, out, s);
     if (!get_encode()) return set_last_error(PE_ERR_NO_DEVICE);
     void* tmp_ws = nullptr;
     if (L.ws_bytes > 0 && (!ws || ws_bytes < L.ws_bytes)) {

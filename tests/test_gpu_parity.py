@@ -271,3 +271,17 @@ def test_cta_pair_kernel(eq, s0, s1, monkeypatch):
     check_close(single, ref, torch.float16)
     torch.testing.assert_close(pair, single, rtol=1e-5, atol=1e-5)
     assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+from llm_patterns import PATTERNS, SMALL, shapes as llm_shapes  # noqa: E402
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("name,eq", PATTERNS, ids=[p[0] for p in PATTERNS])
+def test_llm_patterns(name, eq, dtype):
+    """The reference's LLM contraction patterns (bench_llm_contractions.py) at
+    small sizes, against the CPU oracle."""
+    s0, s1 = llm_shapes(eq, SMALL)
+    a, b = seeded(s0, dtype, 61, "randn"), seeded(s1, dtype, 62, "randn")
+    out = einsum(eq, a.cuda(), b.cuda())
+    check_close(out, oracle.einsum_cpu(eq, a, b), dtype, exact=_is_exact(eq, s0, s1))
