@@ -105,7 +105,7 @@ struct Cfg {
     // buffers of one slot. fp32: the k-steps of a tile rotate over acc_slots
     // (S = 1, 2 or 4) slots that the epilogue adds with IEEE fp32 adds, and
     // 4 / S buffers alternate between tiles.
-    static constexpr int SLOTS = F32 ? 4 : 2;
+    static constexpr int SLOTS = (F32 && BN == 128) ? 4 : 2;
     static constexpr int TMEM_COLS = SLOTS * BN;
     // fp32: warps computing the tf32 small halves in shared memory (0 when
     // the variant is only used with both halves precomputed)
@@ -793,6 +793,13 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
 // that both give bit-identical results.
 // fp16 wide tiles run as CTA pairs (tcgen05 cta_group::2, 256x256 tiles)
 // unless PE_GEMM_PAIRS=0.
+// fp32 256-column tiles when both tf32 small halves are precomputed, unless
+// PE_GEMM_WIDE_FP32=0.
+int wide_fp32_enabled() {
+    const char* e = getenv("PE_GEMM_WIDE_FP32");
+    return (e && e[0] == '0') ? 0 : 1;
+}
+
 int pairs_enabled() {
     const char* e = getenv("PE_GEMM_PAIRS");
     return (e && e[0] == '0') ? 0 : 1;
@@ -1305,7 +1312,20 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
             return set_last_error(PE_ERR_UNSUPPORTED);
         // both small halves precomputed: the split warps have nothing to do, so
         // spend the threads on epilogue warps instead (output-bound shapes)
-        rc = (g.a_pre && g.b_pre) ? launch_gemm<Cfg<128, true, 8, false, 0>>(g, s) : launch_gemm<Cfg<128, true>>(g, s);
+        const int64_t tiles256 = pl->I * ((pl->L0 + 127) / 128) * ((pl->L1 + 255) / 256);
+        if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256 >= num_sms() &&
+            wide_fp32_enabled()) {
+            // wide tiles halve the tf32 MMA count per output column block
+            OperandView vbs = vb;
+            vbs.base = (uint8_t*)ws + L.bs_off;
+            if (!encode_operand(&g.tmb, vb, true, 256) || !encode_operand(&g.tmbs, vbs, true, 256))
+                return set_last_error(PE_ERR_UNSUPPORTED);
+            rc = launch_gemm<Cfg<256, true, 8, false, 0>>(g, s);
+        } else if (g.a_pre && g.b_pre) {
+            rc = launch_gemm<Cfg<128, true, 8, false, 0>>(g, s);
+        } else {
+            rc = launch_gemm<Cfg<128, true>>(g, s);
+        }
     } else {
         // pairs halve each SM's operand traffic, which pays off where the
         // mainloop dominates (long K); output-bound short-K shapes stay single

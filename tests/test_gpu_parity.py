@@ -285,3 +285,19 @@ def test_llm_patterns(name, eq, dtype):
     a, b = seeded(s0, dtype, 61, "randn"), seeded(s1, dtype, 62, "randn")
     out = einsum(eq, a.cuda(), b.cuda())
     check_close(out, oracle.einsum_cpu(eq, a, b), dtype, exact=_is_exact(eq, s0, s1))
+
+
+@pytest.mark.parametrize("eq,s0,s1", [("tn, sn -> ts", (2048, 128), (4096, 128)),
+                                      ("ij, jk -> ik", (1000, 96), (96, 5000))])
+def test_fp32_wide_tiles(eq, s0, s1, monkeypatch):
+    """fp32 with both tf32 small halves precomputed on 256-column tiles, against
+    the oracle and the 128-column kernel."""
+    a, b = seeded(s0, torch.float32, 71, "randn"), seeded(s1, torch.float32, 72, "randn")
+    ref = oracle.einsum_cpu(eq, a, b)
+    monkeypatch.setenv("PE_GEMM_WIDE_FP32", "1")
+    wide = einsum(eq, a.cuda(), b.cuda())
+    check_close(wide, ref, torch.float32)
+    monkeypatch.setenv("PE_GEMM_WIDE_FP32", "0")
+    narrow = einsum(eq, a.cuda(), b.cuda())
+    check_close(narrow, ref, torch.float32)
+    assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
