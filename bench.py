@@ -293,6 +293,58 @@ def run_callers_suite(args):
                           "speedup_vs_torch": round(mt / ms, 3), "rel_frobenius_vs_torch_fp32": err}))
 
 
+def run_permute_suite(args):
+    """Transpose family (reference include/pto_einsum_transpose.h, benchmarks/base/
+    bench_transpose.py): pe_permute on large N-D permutes, GB/s (read + write) vs the
+    measured copy roof and vs torch's permute().contiguous(); plus the reference's
+    transposing einsum 'ai,ja->ij' at a large size."""
+    import ctypes
+    from pto_einsum import EinsumBuilder, _core
+    lib = _core.core_lib()
+
+    class Plan(ctypes.Structure):
+        _fields_ = [("dtype", ctypes.c_int32), ("dims", ctypes.c_int32),
+                    ("from_shape", ctypes.c_int64 * 8), ("perm", ctypes.c_int32 * 8)]
+    dev = torch.device("cuda", 0)
+    hbm, _, _ = peaks()
+    steps, warmup = max(args.steps // 10, 10), args.warmup
+    cases = [((16, 4096, 32, 128), (0, 2, 1, 3)), ((8192, 8192), (1, 0)), ((64, 1024, 1024), (0, 2, 1)),
+             ((16, 4096, 32, 128), (0, 2, 3, 1)), ((8, 2048, 32, 128), (3, 1, 0, 2))]
+    for dt in (torch.float16, torch.float32):
+        for shape, perm in cases:
+            x = torch.randn(shape, device=dev).to(dt)
+            out = torch.empty([shape[i] for i in perm], device=dev, dtype=dt)
+            pl = Plan()
+            pl.dtype = 0 if dt == torch.float32 else 1
+            pl.dims = len(shape)
+            for i, (d, q) in enumerate(zip(shape, perm)):
+                pl.from_shape[i] = d
+                pl.perm[i] = q
+            st = torch.cuda.current_stream(dev).cuda_stream
+
+            def ours():
+                rc = lib.pe_permute(ctypes.byref(pl), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                    ctypes.c_void_p(st))
+                assert rc == 0
+            ms = _time(ours, steps, warmup)
+            mt = _time(lambda: x.permute(perm).contiguous(), steps, warmup)
+            ok = torch.equal(out, x.permute(perm).contiguous())
+            nbytes = 2 * x.numel() * x.element_size()
+            print(json.dumps({"suite": "permute", "shape": shape, "perm": perm, "dtype": str(dt).split(".")[-1],
+                              "ms": round(ms, 4), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                              "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / hbm, 3),
+                              "torch_GB/s": round(nbytes / (mt * 1e-3) / 1e9, 1), "exact": ok}))
+        n = 8192
+        a = torch.rand(n, n, device=dev).to(dt)
+        b = torch.rand(n, n, device=dev).to(dt)
+        run = EinsumBuilder("ai, ja -> ij", [(n, n), (n, n)], dt).build()
+        ms = _time(lambda: run(a, b), max(steps // 4, 3), warmup)
+        mt = _time(lambda: torch.einsum("ai,ja->ij", a, b), max(steps // 4, 3), warmup)
+        print(json.dumps({"suite": "permute", "op": "einsum ai,ja->ij (transposed operands)", "n": n,
+                          "dtype": str(dt).split(".")[-1], "ms": round(ms, 4), "TFLOP/s": round(2 * n**3 / (ms * 1e-3) / 1e12, 1),
+                          "torch_ms": round(mt, 4)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,7 +354,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=6)
-    ap.add_argument("--suite", default=None, choices=["callers"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute"],
                     help="instead of the one-line benchmark: time the LLM contraction patterns and the "
                          "linear-attention chain against torch.einsum (one JSON line per op)")
     ap.add_argument("--shrink", type=int, default=1,
@@ -325,6 +377,9 @@ def main():
         return
     if args.suite == "callers":
         run_callers_suite(args)
+        return
+    if args.suite == "permute":
+        run_permute_suite(args)
         return
 
     dist = None

@@ -1,5 +1,6 @@
 """CUDA path vs the CPU oracle on the reference's parity corpus (GPU)."""
 import ctypes
+import math
 import zlib
 
 import numpy as np
@@ -190,6 +191,11 @@ TRANSPOSE_CASES = [  # tests/test_transpose.py:108-162 (shape, perm)
     ((10, 20), (1, 0)), ((8, 12), (1, 0)), ((256, 256), (1, 0)), ((512, 64), (1, 0)), ((80, 256), (1, 0)),
     ((144, 208), (1, 0)), ((201, 199), (1, 0)), ((333, 257), (1, 0)), ((257, 257), (1, 0)),
     ((2, 3, 4, 5), (3, 1, 0, 2)), ((8, 33, 2, 65), (0, 3, 1, 2)),
+    # kernel-path coverage: vector run copy with outer decode, odd runs,
+    # 128-wide 2-byte tiles with ragged edges, narrow destination axis
+    ((4, 40, 8, 16), (0, 2, 1, 3)), ((4, 6, 5, 7), (0, 2, 1, 3)), ((136, 392), (1, 0)),
+    ((3, 200, 136), (0, 2, 1)), ((2, 64, 32, 128), (3, 1, 0, 2)), ((2, 24, 4, 136), (0, 2, 3, 1)),
+    ((40, 24, 16), (1, 2, 0)), ((6, 48, 8, 24), (1, 3, 0, 2)),
 ]
 
 
@@ -213,6 +219,29 @@ def test_permute_kernel(shape, perm, dtype):
                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 0
     assert torch.equal(out, x.permute(perm).contiguous())
+
+
+def _fuzz_permute_cases(n=24, seed=5):
+    import random
+    rng = random.Random(seed)
+    cases = []
+    for _ in range(n):
+        nd = rng.randint(2, 5)
+        shape = tuple(rng.choice([1, 2, 3, 8, 16, 24, 40, 64, 72, 136]) for _ in range(nd))
+        while math.prod(shape) > (1 << 21):
+            shape = tuple(max(1, v // 2) for v in shape)
+        perm = list(range(nd))
+        rng.shuffle(perm)
+        cases.append((shape, tuple(perm)))
+    return cases
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("shape,perm", _fuzz_permute_cases())
+def test_permute_kernel_fuzz(shape, perm, dtype):
+    """Seeded random shapes and permutations through every copy path (run copy,
+    tiled transposes with and without widened axes, element copy): exact."""
+    test_permute_kernel(shape, perm, dtype)
 
 
 def test_zero_size_and_degenerate():
