@@ -249,7 +249,7 @@ def _time(fn, steps, warmup):
 
 
 def run_callers_suite(args):
-    """SURVEY 8(f) chained callers: the reference's LLM contraction patterns and the
+    """Chained callers: the reference's LLM contraction patterns and the
     linear-attention chain (bench_linear_attention.py), B200 vs torch.einsum."""
     from llm_patterns import LARGE, PATTERNS, shapes
     from pto_einsum import EinsumBuilder
@@ -345,6 +345,76 @@ def run_permute_suite(args):
                           "torch_ms": round(mt, 4)}))
 
 
+def run_gdn_suite(args):
+    """GDN stage backends (the reference's benchmarks/complex/gdn/bench_gdn_4way.py
+    workloads: N_seq x L_seg in {1,2} x {512,1024}, H=32 value heads, Hg=16 key heads,
+    head dim 128, chunk 128, fp32). Per stage: median device time with a 256 MB L2
+    flush before each sample, torch.einsum backend vs this library's kernels on the
+    same glue; then the whole forward eager and as one CUDA graph. Error = relative
+    Frobenius vs the same pipeline in float64 (torch)."""
+    from pto_einsum.gdn import GDNChunked, GDNGraph, random_gdn_inputs
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    iters = max(args.steps // 10, 10)
+
+    def med(fn, warmup=3):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return ((a - b).norm() / b.norm()).item()
+
+    H, Hg, D, C = 32, 16, 128, 128
+    for n_seq, l_seg in [(1, 512), (2, 512), (1, 1024), (2, 1024)]:
+        T = n_seq * l_seg
+        cu = list(range(0, T + 1, l_seg))
+        q, k, v, g, beta = random_gdn_inputs(T, H, Hg, D, seed=T + n_seq, device=dev)
+        scale = D ** -0.5
+        row = {"suite": "gdn", "N_seq": n_seq, "L_seg": l_seg, "T": T, "H": H, "Hg": Hg, "D": D, "chunk": C,
+               "dtype": "float32"}
+        ref = GDNChunked("torch", chunk=C, dtype=torch.float64)(
+            *(x.double() for x in (q, k, v, g, beta)), scale=scale, cu_seqlens=cu)
+        for name in ("torch", "pto"):
+            m = GDNChunked(name, chunk=C)
+            f = lambda x: m.fold(x, cu)  # noqa: E731
+            qf, kf, vf, gf, bf = f(q), f(k), f(v), f(g), f(beta)
+            gcum = m.cumsum(gf)
+            A = m.kkt(kf, bf, gcum)
+            Ainv = m.solve_tril(A)
+            w, u = m.wy_fast(kf, vf, bf, Ainv, gcum)
+            h, vn, _ = m.chunk_h(kf, w, u, gcum)
+            stages = {
+                "kkt": lambda: m.kkt(kf, bf, gcum),
+                "solve_tril": lambda: m.solve_tril(A),
+                "wy_fast": lambda: m.wy_fast(kf, vf, bf, Ainv, gcum),
+                "chunk_h": lambda: m.chunk_h(kf, w, u, gcum),
+                "chunk_o": lambda: m.chunk_o(qf, kf, vn, h, gcum),
+            }
+            row[f"{name}_stage_ms"] = {st: round(med(fn), 4) for st, fn in stages.items()}
+            row[f"{name}_contraction_stages_ms"] = round(sum(v for st, v in row[f"{name}_stage_ms"].items()
+                                                             if st != "solve_tril"), 4)
+            row[f"{name}_forward_ms"] = round(med(lambda: m(q, k, v, g, beta, scale=scale, cu_seqlens=cu)), 4)
+            graph = GDNGraph(m, q, k, v, g, beta, scale=scale, cu_seqlens=cu)
+            row[f"{name}_forward_graph_ms"] = round(med(lambda: graph(q, k, v, g, beta)), 4)
+            row[f"{name}_rel_err_vs_fp64"] = rel(m(q, k, v, g, beta, scale=scale, cu_seqlens=cu), ref)
+            del graph
+            if name == "pto":
+                m.cleanup()
+        print(json.dumps(row))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -354,7 +424,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=6)
-    ap.add_argument("--suite", default=None, choices=["callers", "permute"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn"],
                     help="instead of the one-line benchmark: time the LLM contraction patterns and the "
                          "linear-attention chain against torch.einsum (one JSON line per op)")
     ap.add_argument("--shrink", type=int, default=1,
@@ -380,6 +450,9 @@ def main():
         return
     if args.suite == "permute":
         run_permute_suite(args)
+        return
+    if args.suite == "gdn":
+        run_gdn_suite(args)
         return
 
     dist = None

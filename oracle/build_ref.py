@@ -1,7 +1,7 @@
 """Compile the reference's own CPU libraries into oracle/_ref/ (TEST
 INFRASTRUCTURE ONLY; run in a container where the reference checkout exists).
 
-    python oracle/build_ref.py [--reference /root/reference]
+    python oracle/build_ref.py [--reference <reference checkout>]
 
 For every spec in ref_specs.SPECS this runs the reference planner and code
 generator (src/pto_einsum/builder.py:555-683, device="cpu") and its compile

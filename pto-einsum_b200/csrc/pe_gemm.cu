@@ -859,26 +859,42 @@ __global__ void __launch_bounds__(256) small_contract(const T* __restrict__ A, c
 }
 
 // tf32 "small" half of fp32 data: y = x - (x with its low 13 mantissa bits
-// cleared). x - trunc(x) is exact in fp32.
-__global__ void __launch_bounds__(256) tf32_small(const float* __restrict__ x, float* __restrict__ y, int64_t n) {
+// cleared). x - trunc(x) is exact in fp32. Up to two operands per launch
+// (blockIdx.y selects the range).
+struct SmallRange {
+    const float* x;
+    float* y;
+    int64_t n;
+};
+
+__global__ void __launch_bounds__(256) tf32_small(SmallRange r0, SmallRange r1) {
+    const SmallRange r = blockIdx.y ? r1 : r0;
+    const float* __restrict__ x = r.x;
+    float* __restrict__ y = r.y;
+    const int64_t n = r.n;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
     const int64_t n4 = n / 4;
     for (int64_t v = i; v < n4; v += step) {
         const float4 a = reinterpret_cast<const float4*>(x)[v];
-        float4 r;
-        r.x = a.x - __uint_as_float(__float_as_uint(a.x) & 0xFFFFE000u);
-        r.y = a.y - __uint_as_float(__float_as_uint(a.y) & 0xFFFFE000u);
-        r.z = a.z - __uint_as_float(__float_as_uint(a.z) & 0xFFFFE000u);
-        r.w = a.w - __uint_as_float(__float_as_uint(a.w) & 0xFFFFE000u);
-        reinterpret_cast<float4*>(y)[v] = r;
+        float4 o;
+        o.x = a.x - __uint_as_float(__float_as_uint(a.x) & 0xFFFFE000u);
+        o.y = a.y - __uint_as_float(__float_as_uint(a.y) & 0xFFFFE000u);
+        o.z = a.z - __uint_as_float(__float_as_uint(a.z) & 0xFFFFE000u);
+        o.w = a.w - __uint_as_float(__float_as_uint(a.w) & 0xFFFFE000u);
+        reinterpret_cast<float4*>(y)[v] = o;
     }
     for (int64_t e = 4 * n4 + i; e < n; e += step) y[e] = x[e] - __uint_as_float(__float_as_uint(x[e]) & 0xFFFFE000u);
 }
 
-int tf32_small_launch(const void* x, void* y, int64_t n, cudaStream_t s) {
-    int64_t blocks = (n / 4 + 255) / 256 + 1, cap = (int64_t)num_sms() * 8;
-    tf32_small<<<(int)std::min(blocks, cap), 256, 0, s>>>((const float*)x, (float*)y, n);
+// a.n or b.n may be 0 (operand not precomputed); nothing launches if both are.
+int tf32_small_launch(SmallRange a, SmallRange b, cudaStream_t s) {
+    if (a.n == 0) std::swap(a, b);
+    if (a.n == 0) return PE_OK;
+    const int ny = b.n ? 2 : 1;
+    const int64_t nmax = std::max(a.n, b.n);
+    int64_t blocks = (nmax / 4 + 255) / 256 + 1, cap = (int64_t)num_sms() * 8 / ny;
+    tf32_small<<<dim3((unsigned)std::min(blocks, cap), ny), 256, 0, s>>>(a, b);
     count_launch();
     return check_cuda(cudaGetLastError());
 }
@@ -1050,7 +1066,10 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
     }
     // fp32 operands that are small next to the output get their tf32 small
     // halves computed once by a streaming pass instead of by the split warps
-    // for every tile that reads them (4a: 4 MB operands, 268 MB output).
+    // for every tile that reads them (4a: 4 MB operands, 268 MB output). An
+    // operand read by a single tile along the other free dimension gains
+    // nothing from the pass (it would only add a launch and a write + read of
+    // the halves), so it keeps the in-kernel split.
     if (es == 4) {
         int64_t n0e = 1, n1e = 1;
         for (int a = 0; a < pl->rank0; ++a) n0e *= pl->shape0[a];
@@ -1058,12 +1077,12 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
         L->n_in0 = n0e;
         L->n_in1 = n1e;
         const int64_t cap = (int64_t)16 << 20;  // elements (64 MB)
-        if (L->a.direct && n0e <= cap) {
+        if (L->a.direct && n0e <= cap && L1 > 128) {
             L->a_pre = true;
             L->as_off = off;
             off += ((size_t)n0e * 4 + 255) & ~(size_t)255;
         }
-        if (L->b.direct && n1e <= cap) {
+        if (L->b.direct && n1e <= cap && L0 > 128) {
             L->b_pre = true;
             L->bs_off = off;
             off += ((size_t)n1e * 4 + 255) & ~(size_t)255;
@@ -1290,10 +1309,10 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
         // more slots for long contractions: fewer accumulation steps per slot
         const int64_t kit = (pl->C + 31) / 32;
         g.acc_slots = kit >= 32 ? 4 : (kit >= 8 ? 2 : 1);
+        SmallRange ra{nullptr, nullptr, 0}, rb{nullptr, nullptr, 0};
         if (L.a_pre) {
             void* sm = (uint8_t*)ws + L.as_off;
-            rc = tf32_small_launch(in0, sm, L.n_in0, s);
-            if (rc) return rc;
+            ra = SmallRange{(const float*)in0, (float*)sm, L.n_in0};
             OperandView v = va;
             v.base = sm;
             if (!encode_operand(&g.tmas, v, true, 128)) return set_last_error(PE_ERR_UNSUPPORTED);
@@ -1301,13 +1320,14 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
         }
         if (L.b_pre) {
             void* sm = (uint8_t*)ws + L.bs_off;
-            rc = tf32_small_launch(in1, sm, L.n_in1, s);
-            if (rc) return rc;
+            rb = SmallRange{(const float*)in1, (float*)sm, L.n_in1};
             OperandView v = vb;
             v.base = sm;
             if (!encode_operand(&g.tmbs, v, true, 128)) return set_last_error(PE_ERR_UNSUPPORTED);
             g.b_pre = 1;
         }
+        rc = tf32_small_launch(ra, rb, s);
+        if (rc) return rc;
         if (!encode_operand(&g.tma, va, true, 128) || !encode_operand(&g.tmb, vb, true, 128))
             return set_last_error(PE_ERR_UNSUPPORTED);
         // both small halves precomputed: the split warps have nothing to do, so

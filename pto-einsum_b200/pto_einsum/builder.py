@@ -232,7 +232,9 @@ class EinsumBuilder:
         self.lib.run_einsum.restype = None
         self.lib.run_einsum_setup.argtypes = [ctypes.c_void_p]
         self.lib.run_einsum_setup.restype = ctypes.c_void_p
-        self.lib.run_einsum_exec.argtypes = [P(T), P(T), fp, ctypes.c_void_p, ctypes.c_void_p]
+        # exec is the per-call hot path: plain addresses (ints) avoid building
+        # ctypes pointer objects on every call; pointer instances are accepted too
+        self.lib.run_einsum_exec.argtypes = [ctypes.c_void_p] * 5
         self.lib.run_einsum_exec.restype = None
         self.lib.run_einsum_teardown.argtypes = [ctypes.c_void_p]
         self.lib.run_einsum_teardown.restype = None
@@ -268,36 +270,53 @@ class EinsumBuilder:
         self._splitk = False if (r['elementwise'] or r['broadcast']) else self._splitk_eligible()
         out_shape = tuple(r['out_shape'])
 
+        shapes = (tuple(self.input_shapes[0]), tuple(self.input_shapes[1]))
+        dtype = self.dtype
+        swap = self._swap_operands
+        exec_fn = self.lib.run_einsum_exec
+        last_error = self.lib.run_einsum_last_error
+
         def run(*operands):
             if len(operands) != 2:
                 raise ValueError("Expected exactly two operands.")
             inp0, inp1 = operands
-            if tuple(inp0.shape) != tuple(self.input_shapes[0]) or tuple(inp1.shape) != tuple(self.input_shapes[1]):
+            if inp0.shape != shapes[0] or inp1.shape != shapes[1]:
                 raise ValueError(
                     f"Input shapes {inp0.shape} and {inp1.shape} do not match built shapes {self.input_shapes}.")
-            if inp0.dtype != self.dtype or inp1.dtype != self.dtype:
+            if inp0.dtype != dtype or inp1.dtype != dtype:
                 raise TypeError(
-                    f"Input datatypes {inp0.dtype} and {inp1.dtype} do not match built datatype {self.dtype}.")
-            if inp0.device.type != 'cuda' or inp1.device != inp0.device:
+                    f"Input datatypes {inp0.dtype} and {inp1.dtype} do not match built datatype {dtype}.")
+            dev = inp0.device
+            if dev.type != 'cuda' or inp1.device != dev:
                 raise ValueError(
-                    f"pto_einsum: both operands must be on the same CUDA device (got {inp0.device}, {inp1.device})")
+                    f"pto_einsum: both operands must be on the same CUDA device (got {dev}, {inp1.device})")
             if not inp0.is_contiguous():
                 inp0 = inp0.contiguous()
             if not inp1.is_contiguous():
                 inp1 = inp1.contiguous()
-            if self._swap_operands:
+            if swap:
                 inp0, inp1 = inp1, inp0
-            dev = inp0.device
             out = torch.empty(out_shape, dtype=torch.float32, device=dev)
             if out.numel() == 0:
                 return out
-            stream = torch.cuda.current_stream(dev).cuda_stream
-            ws = self.workspace(dev, stream)
-            with torch.cuda.device(dev):
-                self.lib.run_einsum_exec(self._ptr(inp0, self.c_type), self._ptr(inp1, self.c_type),
-                                         self._ptr(out, ctypes.c_float), ctypes.c_void_p(ws),
-                                         ctypes.c_void_p(stream))
-            self._check("run_einsum_exec")
+            if self.lib is None:
+                raise RuntimeError("pto_einsum: runner called after cleanup()")
+            idx = dev.index
+            wss = self._workspace
+            ws = wss.get(idx) if wss else None
+            if idx == torch.cuda.current_device():
+                stream = torch.cuda.current_stream().cuda_stream
+                if ws is None:
+                    ws = self.workspace(dev, stream)
+                exec_fn(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
+            else:
+                stream = torch.cuda.current_stream(dev).cuda_stream
+                if ws is None:
+                    ws = self.workspace(dev, stream)
+                with torch.cuda.device(dev):
+                    exec_fn(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
+            if last_error():
+                self._check("run_einsum_exec")
             return out
 
         return run

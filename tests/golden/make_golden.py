@@ -1,7 +1,7 @@
 """Generate the golden fixtures from the reference implementation itself.
 
-Run in a container where the reference checkout is present (default
-/root/reference, override with PTO_EINSUM_REFERENCE):
+Run where the reference checkout is present (its path in PTO_EINSUM_REFERENCE,
+or the default below):
 
     python tests/golden/make_golden.py
 
