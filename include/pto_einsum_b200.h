@@ -156,6 +156,12 @@ int pe_last_error(void);
 const char* pe_error_string(int code);
 /* Synchronise `stream`, return and clear the device-side error word. */
 int pe_device_error(void* stream);
+/* Self-test of the device-side failure path: one CTA waits on a pipeline barrier
+ * that nothing arrives on, through the same bounded wait every GEMM stage uses,
+ * with a limit of `timeout_ns` (at most 100 ms). Returns the device error word the
+ * expired wait recorded (PE_ERR_TIMEOUT | site << 8, site 15) and clears it; the
+ * CUDA context stays usable. Synchronises `stream`. */
+int pe_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
 /* Number of core kernels this process has launched (for launch accounting). */
 int64_t pe_launch_count(void);
 /* Block the host until all work queued on `stream` finished. */

@@ -160,6 +160,10 @@ int pe_device_error(void* stream) {
     return v;
 }
 
+int pe_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+    return wait_timeout_selftest(timeout_ns, (cudaStream_t)stream);
+}
+
 int pe_stream_synchronize(void* stream) {
     return check_cuda(cudaStreamSynchronize((cudaStream_t)stream));
 }

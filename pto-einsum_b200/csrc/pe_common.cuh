@@ -85,14 +85,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for phase `parity` of `bar`. Returns false (and raises *abort)
 // when the CTA already aborted or the wait exceeded the timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int where) {
+                                          int where, uint64_t timeout_ns = PE_WAIT_TIMEOUT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer();
     while (true) {
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer() - t0 > PE_WAIT_TIMEOUT_NS) {
+        if (globaltimer() - t0 > timeout_ns) {
             *abort_flag = 1;
             record_error(PE_ERR_TIMEOUT | (where << 8));
             return false;

@@ -1363,6 +1363,43 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
 
 }  // namespace
 
+// Self-test of the bounded-wait path: one CTA waits on an mbarrier that nothing
+// arrives on, through the same mbar_wait the GEMM pipeline uses, with a short
+// limit. The wait gives up, records PE_ERR_TIMEOUT (site 15) in the device error
+// word and the kernel returns normally, so the context stays usable.
+__global__ void wait_timeout_probe(uint64_t timeout_ns, int* result) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_sh;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_sh = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait(smem_u32(&bar), 0, &abort_sh, 15, timeout_ns);
+        *result = ok ? 1 : 0;
+    }
+}
+
+int wait_timeout_selftest(uint64_t timeout_ns, cudaStream_t s) {
+    if (timeout_ns > 100000000ull) return set_last_error(PE_ERR_INVALID);  // at most 100 ms
+    int* d = nullptr;
+    int rc = check_cuda(cudaMallocAsync(&d, sizeof(int), s));
+    if (rc) return rc;
+    wait_timeout_probe<<<1, 32, 0, s>>>(timeout_ns, d);
+    count_launch();
+    int h = -1;
+    rc = check_cuda(cudaGetLastError());
+    if (!rc) rc = check_cuda(cudaMemcpyAsync(&h, d, sizeof(int), cudaMemcpyDeviceToHost, s));
+    if (!rc) rc = check_cuda(cudaStreamSynchronize(s));
+    cudaFreeAsync(d, s);
+    if (rc) return rc;
+    const int code = gemm_device_error(true);
+    set_last_error(PE_OK);
+    return h == 0 ? code : 0;  // the wait must not have succeeded
+}
+
 int gemm_device_error(bool clear) {
     int v = 0, zero = 0;
     if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;

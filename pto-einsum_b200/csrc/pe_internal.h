@@ -31,5 +31,6 @@ int contract(const pe_contract_plan* plan, const void* in0, const void* in1, flo
 
 // Read (and optionally clear) the device error word of the GEMM kernels.
 int gemm_device_error(bool clear);
+int wait_timeout_selftest(uint64_t timeout_ns, cudaStream_t s);
 
 }  // namespace pe

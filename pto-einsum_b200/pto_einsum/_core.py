@@ -48,6 +48,8 @@ def _declare(lib):
     lib.pe_device_error.restype = c.c_int
     lib.pe_device_error.argtypes = [c.c_void_p]
     lib.pe_launch_count.restype = c.c_int64
+    lib.pe_selftest_wait_timeout.argtypes = [c.c_uint64, c.c_void_p]
+    lib.pe_selftest_wait_timeout.restype = c.c_int
     lib.pe_version.restype = c.c_char_p
     lib.pe_stream_synchronize.argtypes = [c.c_void_p]
     lib.pe_elementwise_mul.argtypes = [c.c_int32, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_void_p]
