@@ -66,6 +66,7 @@ struct GemmArgs {
     int acc_slots;   // fp32: accumulator slots per tile (1, 2 or 4)
     int ksplit;      // work units per output tile (split-K), >= 1
     int kper;        // k-iterations per unit
+    int sk_q;        // stream-K: k-iterations per CTA (group) over the flattened (tile, k) space; 0 = off
     int nbatch;      // I: batch count of the plan (split-K partials use batch i + sp*I)
     int raw_big;     // fp32: feed x unmasked as the big part (tensor core truncation)
     float* out;
@@ -147,6 +148,37 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity) {
     }
 }
 
+// The idx-th work unit of CTA (group) `unit0` of `ustep`: output tile t, its
+// k-iteration range [kb_lo, kb_hi) and the partial slab sp it writes.
+// Split-K (sk_q == 0): units are (tile, equal k-slice) pairs dealt round-robin.
+// Stream-K (sk_q > 0): CTA c owns the flattened iterations [c*Q, (c+1)*Q) of
+// the (tile, k) space and emits one partial per tile it touches; sp numbers the
+// segments of a tile by the CTA boundaries inside it, so a deterministic
+// reduction can sum them in order.
+__device__ __forceinline__ bool work_unit(const GemmArgs& g, int unit0, int ustep, int idx, int& t, int& sp,
+                                          int& kb_lo, int& kb_hi) {
+    if (g.sk_q > 0) {
+        const int64_t q = g.sk_q;
+        const int64_t lo = (int64_t)unit0 * q;
+        const int64_t hi = min(lo + q, (int64_t)g.tiles * g.kiters);
+        const int64_t tt = lo / g.kiters + idx;
+        const int64_t base = tt * g.kiters;
+        if (base >= hi) return false;
+        t = (int)tt;
+        kb_lo = (int)(lo > base ? lo - base : 0);
+        kb_hi = (int)min(hi - base, (int64_t)g.kiters);
+        sp = (int)((base + kb_lo) / q - base / q);
+        return true;
+    }
+    const int u = unit0 + idx * ustep;
+    if (u >= g.tiles * g.ksplit) return false;
+    t = u / g.ksplit;
+    sp = u - t * g.ksplit;
+    kb_lo = sp * g.kper;
+    kb_hi = min(g.kiters, kb_lo + g.kper);
+    return true;
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
     extern __shared__ uint8_t smem_raw[];
@@ -210,9 +242,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued_mask = 0, issued_par = 0;
-            for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
-                const int t = u / g.ksplit, sp = u - t * g.ksplit;
-                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
+            int t, sp, kb_lo, kb_hi;
+            for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
                 const int i = t / per_batch, r = t - i * per_batch;
                 const int m0 = (r / g.nblk) * C::TM + (int)rank * C::BM;   // this CTA's A rows
                 const int n0 = (r % g.nblk) * C::BN + (int)rank * (C::BN - C::BNL);  // its B columns
@@ -288,9 +319,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const uint32_t a_sbo = a_lay == 1 ? 512 : 1024, b_sbo = b_lay == 1 ? 512 : 1024;
             int stage = 0, acc = 0;
             uint32_t phase = 0, acc_phase = 0;
-            for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
-                const int t = u / g.ksplit, sp = u - t * g.ksplit;
-                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
+            int t, sp, kb_lo, kb_hi;
+            for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
                 if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
                 tc_fence_after();
                 const uint32_t dbuf = tmem_base + (uint32_t)(acc * S * C::BN);
@@ -355,9 +385,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         int acc = 0;
         uint32_t acc_phase = 0;
         uint8_t* stage_buf = epi + ew * C::EBUF * 4096;
-        for (int u = unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
-            const int t = u / g.ksplit, sp = u - t * g.ksplit;
-            const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
+        int t, sp, kb_lo, kb_hi;
+        for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
             const int i = t / per_batch, r = t - i * per_batch;
             const int m0 = (r / g.nblk) * C::TM + (int)rank * C::BM, n0 = (r % g.nblk) * C::BN;
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
@@ -479,9 +508,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int jhi = g.b_pre ? C::A_BYTES / 16 : C::TX_BYTES / 16;
         int stage = 0;
         uint32_t phase = 0;
-        for (int u = split_done_by_tma ? g.tiles * g.ksplit : unit0; u < g.tiles * g.ksplit && !*abort_flag; u += ustep) {
-                const int t = u / g.ksplit, sp = u - t * g.ksplit;
-                const int kb_lo = sp * g.kper, kb_hi = min(g.kiters, kb_lo + g.kper);
+        int t, sp, kb_lo, kb_hi;
+        for (int idx = 0; !split_done_by_tma && !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi);
+             ++idx) {
             bool ok = true;
             for (int kb = kb_lo; kb < kb_hi; ++kb) {
                 if (!mbar_wait(full(stage), phase, abort_flag, 5)) {
@@ -751,7 +780,9 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
     g.mblk = (int)((g.M + C::TM - 1) / C::TM);
     g.nblk = (int)((g.N + C::BN - 1) / C::BN);
     g.kiters = (int)((g.K + C::BK - 1) / C::BK);
-    if (g.ksplit <= 1 || g.kiters < 2) {
+    if (g.sk_q > 0) {
+        g.kper = g.kiters;  // unused: stream-K units come from sk_q
+    } else if (g.ksplit <= 1 || g.kiters < 2) {
         g.ksplit = 1;
         g.kper = g.kiters;
     } else {
@@ -761,6 +792,15 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
     int64_t tiles = (int64_t)g.mblk * g.nblk * (int64_t)g.tiles;  // g.tiles holds I on entry
     if (tiles > 0x7FFFFFFF) return set_last_error(PE_ERR_UNSUPPORTED);
     g.tiles = (int)tiles;
+    if (g.sk_q > 0) {
+        // the plan's slab count must cover every tile's segments
+        if (C::PAIR || (g.kiters + g.sk_q - 1) / g.sk_q + 1 > g.ksplit) return set_last_error(PE_ERR_INVALID);
+        const int64_t grid = (tiles * g.kiters + g.sk_q - 1) / g.sk_q;
+        if (grid > num_sms()) return set_last_error(PE_ERR_INVALID);
+        gemm_kernel<C><<<(int)grid, C::THREADS, C::SMEM, s>>>(g);
+        count_launch();
+        return check_cuda(cudaGetLastError());
+    }
     if constexpr (C::PAIR) {
         // one cluster of two CTAs per tile pair, persistent over the SMs
         const int pairs = (int)std::min<int64_t>(tiles * g.ksplit, num_sms() / 2);
@@ -798,6 +838,18 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
 int wide_fp32_enabled() {
     const char* e = getenv("PE_GEMM_WIDE_FP32");
     return (e && e[0] == '0') ? 0 : 1;
+}
+
+int thin_enabled() {
+    const char* e = getenv("PE_THIN");
+    return (e && e[0] == '0') ? 0 : 1;
+}
+
+int streamk_mode() {
+    const char* e = getenv("PE_GEMM_STREAMK");
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '2') return 2;
+    return 1;
 }
 
 int pairs_enabled() {
@@ -858,6 +910,115 @@ __global__ void __launch_bounds__(256) small_contract(const T* __restrict__ A, c
     }
 }
 
+// Thin contraction: outputs with a free dimension of at most 4 whose
+// contraction is one contiguous run in both operands (dot products,
+// matrix-vector products, their batched forms). Work item = (output element,
+// chunk of the contraction), one warp each: 16-byte loads of both operands,
+// four fp32 accumulators per lane (fused multiply-add), then a fixed shuffle
+// tree, so results are run-to-run identical. With several chunks the partial
+// sums go to `part` ([chunk][output]) and a fixed-order reduction adds them.
+struct ThinArgs {
+    SimtArgs s;          // output decode; s.C = contraction length
+    int64_t chunk;       // contraction elements per work item (multiple of 64)
+    int nchunk;
+    int aligned;         // both base pointers 16-byte aligned
+};
+
+template <typename T>
+__device__ __forceinline__ void fma_vec(const uint4& x, const uint4& y, float& a0, float& a1) {
+    if constexpr (sizeof(T) == 4) {
+        a0 = fmaf(__uint_as_float(x.x), __uint_as_float(y.x), a0);
+        a1 = fmaf(__uint_as_float(x.y), __uint_as_float(y.y), a1);
+        a0 = fmaf(__uint_as_float(x.z), __uint_as_float(y.z), a0);
+        a1 = fmaf(__uint_as_float(x.w), __uint_as_float(y.w), a1);
+    } else {
+        const __half2* hx = reinterpret_cast<const __half2*>(&x);
+        const __half2* hy = reinterpret_cast<const __half2*>(&y);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float2 fx = __half22float2(hx[q]), fy = __half22float2(hy[q]);
+            a0 = fmaf(fx.x, fy.x, a0);
+            a1 = fmaf(fx.y, fy.y, a1);
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) thin_contract(const T* __restrict__ A, const T* __restrict__ B,
+                                                     float* __restrict__ out, float* __restrict__ part,
+                                                     ThinArgs p) {
+    constexpr int VEC = 16 / sizeof(T);
+    const int lane = threadIdx.x & 31;
+    const int64_t nwork = p.s.n * p.nchunk;
+    const int64_t wstep = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < nwork; w += wstep) {
+        const int64_t e = w / p.nchunk;
+        const int j = (int)(w - e * p.nchunk);
+        uint32_t rem = (uint32_t)e;
+        int64_t ao = 0, bo = 0;
+        for (int a = p.s.nd - 1; a >= 0; --a) {
+            const uint32_t q = fdiv(rem, p.s.div[a]);
+            const uint32_t idx = rem - q * p.s.div[a].div;
+            rem = q;
+            ao += (int64_t)idx * p.s.sa[a];
+            bo += (int64_t)idx * p.s.sb[a];
+        }
+        const int64_t c0 = (int64_t)j * p.chunk;
+        const int64_t c1 = min(p.s.C, c0 + p.chunk);
+        const T* a = A + ao;
+        const T* b = B + bo;
+        float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+        int64_t c = c0;
+        if (p.aligned && (ao % VEC) == 0 && (bo % VEC) == 0) {
+            // two 16-byte vectors per operand and lane in flight per step
+            for (; c + 64 * VEC <= c1; c += 64 * VEC) {
+                const uint4 x0 = __ldcs(reinterpret_cast<const uint4*>(a + c + lane * VEC));
+                const uint4 y0 = __ldcs(reinterpret_cast<const uint4*>(b + c + lane * VEC));
+                const uint4 x1 = __ldcs(reinterpret_cast<const uint4*>(a + c + (32 + lane) * VEC));
+                const uint4 y1 = __ldcs(reinterpret_cast<const uint4*>(b + c + (32 + lane) * VEC));
+                fma_vec<T>(x0, y0, acc0, acc1);
+                fma_vec<T>(x1, y1, acc2, acc3);
+            }
+        }
+        for (c += lane; c < c1; c += 32) acc0 = fmaf((float)a[c], (float)b[c], acc0);
+        float sum = (acc0 + acc1) + (acc2 + acc3);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_down_sync(0xffffffffu, sum, off);
+        if (lane == 0) {
+            if (p.nchunk == 1) out[e] = sum;
+            else part[(int64_t)j * p.s.n + e] = sum;
+        }
+    }
+}
+
+// Thin partials [chunk][output] -> out[output]: one warp per output, lanes
+// take chunks j = lane, lane + 32, ... in order, then a fixed shuffle tree
+// (run-to-run identical).
+__global__ void __launch_bounds__(256) thin_reduce(const float* __restrict__ part, float* __restrict__ out,
+                                                   int64_t n, int nchunk) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wstep = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t e = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); e < n; e += wstep) {
+        float acc = 0.f;
+        for (int j = lane; j < nchunk; j += 32) acc += part[(int64_t)j * n + e];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, off);
+        if (lane == 0) out[e] = acc;
+    }
+}
+
+template <typename T>
+int thin_resident_blocks() {
+    static int n = 0;
+    if (n == 0) {
+        int b = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, thin_contract<T>, 256, 0) != cudaSuccess || b <= 0)
+            b = 4;
+        n = b;
+    }
+    return n;
+}
+
 // tf32 "small" half of fp32 data: y = x - (x with its low 13 mantissa bits
 // cleared). x - trunc(x) is exact in fp32. Up to two operands per launch
 // (blockIdx.y selects the range).
@@ -913,6 +1074,32 @@ __global__ void __launch_bounds__(256) splitk_reduce(const float* __restrict__ p
     }
 }
 
+// Stream-K reduction: element e of tile t sums the nseg(t) partial slabs of
+// that tile's segments in slab order (fixed, so results are run-to-run
+// identical); nseg follows from where the CTA boundaries (multiples of q in
+// the flattened (tile, k) space) fall inside the tile.
+struct SkReduce {
+    int64_t L0, L1, per_batch, q;
+    int nblk, tm, bn, kiters;
+};
+
+__global__ void __launch_bounds__(256) streamk_reduce(const float* __restrict__ part, float* __restrict__ out,
+                                                      int64_t n, SkReduce r, Decode od) {
+    int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    const int64_t plane = r.L0 * r.L1;
+    for (; e < n; e += step) {
+        const int64_t i = e / plane, rem = e - i * plane;
+        const int64_t m = rem / r.L1, nn = rem - m * r.L1;
+        const int64_t t = i * r.per_batch + (m / r.tm) * r.nblk + nn / r.bn;
+        const int64_t base = t * r.kiters;
+        const int ns = (int)((base + r.kiters - 1) / r.q - base / r.q + 1);
+        float acc = part[e];
+        for (int k = 1; k < ns; ++k) acc += part[(int64_t)k * n + e];
+        out[decode_off(od, e)] = acc;
+    }
+}
+
 struct Lowered;
 int splitk_reduce_launch(const float* part, float* out, const Lowered& L, const pe_contract_plan* pl, int ks,
                          cudaStream_t s);
@@ -928,13 +1115,37 @@ struct Lowered {
     int64_t n_in0 = 0, n_in1 = 0;        // raw operand element counts
     int bn = 128;                 // N tile of the chosen kernel
     bool simt = false;            // degenerate shape: streaming kernel instead of the GEMM
+    bool thin = false;            // thin output, contiguous contraction: warp-per-dot kernel
+    int64_t thin_chunk = 0, thin_nchunk = 1;
     int ksplit = 1;               // split-K factor (partials in the workspace when > 1)
+    int64_t sk_q = 0;             // stream-K iterations per CTA (0 = off); ksplit = slab count then
     // group axes
     Axis a_batch[PE_MAX_RANK], a_free[PE_MAX_RANK], a_ct[PE_MAX_RANK];
     Axis b_batch[PE_MAX_RANK], b_free[PE_MAX_RANK], b_ct[PE_MAX_RANK];
     int nb = 0, n0 = 0, n1 = 0, nc = 0;
     OutView out;
 };
+
+// Contraction axes of the plan merged where they are contiguous in both
+// operands (outermost first). Returns the number of merged axes.
+int coalesce_contraction(const Lowered& L, int64_t* ksize, int64_t* ka, int64_t* kb) {
+    int nk = 0;
+    for (int j = 0; j < L.nc; ++j) {
+        if (L.a_ct[j].size == 1) continue;
+        if (nk > 0 && ka[nk - 1] == L.a_ct[j].stride * L.a_ct[j].size &&
+            kb[nk - 1] == L.b_ct[j].stride * L.b_ct[j].size) {
+            ksize[nk - 1] *= L.a_ct[j].size;
+            ka[nk - 1] = L.a_ct[j].stride;
+            kb[nk - 1] = L.b_ct[j].stride;
+        } else {
+            ksize[nk] = L.a_ct[j].size;
+            ka[nk] = L.a_ct[j].stride;
+            kb[nk] = L.b_ct[j].stride;
+            nk++;
+        }
+    }
+    return nk;
+}
 
 bool valid_perm(const int32_t* p, int n) {
     bool seen[PE_MAX_RANK] = {false};
@@ -1030,6 +1241,28 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
         L->ws_bytes = 0;
         return PE_OK;
     }
+    // Thin outputs over a long contraction that is one contiguous run in both
+    // operands (dot products, matrix-vector products): an MMA tile would
+    // compute up to 128x128 products per useful one, so a streaming kernel
+    // with one warp per (output, contraction chunk) reads both operands once.
+    if (std::min(L0, L1) <= 4 && C >= 256 && thin_enabled()) {
+        int64_t ks[PE_MAX_RANK], ka[PE_MAX_RANK], kb[PE_MAX_RANK];
+        const int nk = coalesce_contraction(*L, ks, ka, kb);
+        const int64_t n_out = I * L0 * L1;
+        if (nk == 1 && ka[0] == 1 && kb[0] == 1 && n_out < (1ll << 31)) {
+            const int64_t want = (int64_t)num_sms() * 64 * 4;  // four work items per resident warp
+            int64_t nch = std::max<int64_t>(1, std::min<int64_t>((want + n_out - 1) / n_out, C / 1024));
+            int64_t chunk = ((C + nch - 1) / nch + 63) / 64 * 64;
+            nch = (C + chunk - 1) / chunk;
+            L->thin = true;
+            L->thin_chunk = chunk;
+            L->thin_nchunk = nch;
+            L->a_ws = L->b_ws = false;
+            L->p_off = 0;
+            L->ws_bytes = nch > 1 ? (((size_t)nch * n_out * 4 + 255) & ~(size_t)255) : 0;
+            return PE_OK;
+        }
+    }
     size_t off = 0;
     if (L->a_ws) {
         L->a_off = off;
@@ -1051,16 +1284,35 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
     }
     const int64_t tiles = I * mblk * ((L1 + L->bn - 1) / L->bn);
     const int64_t kiters = (C + (128 / es) - 1) / (128 / es);
+    const double in_bytes = (double)es * (double)C * (double)(I * L0 + I * L1);
+    const double part_bytes = 8.0 * (double)(I * L0 * L1);
+    double best = 1.0;
     if (tiles > 0 && tiles * 2 <= nsm && kiters >= 64) {
-        const double in_bytes = (double)es * (double)C * (double)(I * L0 + I * L1);
-        const double part_bytes = 8.0 * (double)(I * L0 * L1);
-        double best = 1.0;
         for (int ks = 2; ks <= 16 && ks <= kiters / 8; ++ks) {
             const double waves = (double)((tiles * ks + nsm - 1) / nsm) / ks;
             const double cost = waves + ks * part_bytes / in_bytes;
             if (cost < best - 0.02) {
                 best = cost;
                 L->ksplit = ks;
+            }
+        }
+    }
+    // Stream-K: every CTA takes an equal share of the flattened (tile, k)
+    // iterations, so all SMs stay busy whatever the tile count; a tile touched
+    // by several CTAs gets one partial per CTA boundary inside it.
+    // PE_GEMM_STREAMK=0 disables it, =2 forces it wherever it can apply.
+    const int skm = streamk_mode();
+    if (skm && tiles > 0 && tiles < nsm && kiters >= (skm == 2 ? 2 : 64)) {
+        const int64_t total = tiles * kiters;
+        const int64_t ncta = std::min<int64_t>(nsm, total / (skm == 2 ? 2 : 8));
+        if (ncta > tiles) {
+            const int64_t q = (total + ncta - 1) / ncta;
+            const double segs = (double)(tiles + ncta - 1) / (double)tiles;
+            const double cost = (double)q / (double)kiters + segs * part_bytes / in_bytes;
+            if (skm == 2 || cost < best - 0.02) {
+                best = cost;
+                L->sk_q = q;
+                L->ksplit = (int)((kiters + q - 1) / q + 1);
             }
         }
     }
@@ -1133,14 +1385,37 @@ int splitk_reduce_launch(const float* part, float* out, const Lowered& L, const 
     return check_cuda(cudaGetLastError());
 }
 
-int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
-                          float* out, cudaStream_t s) {
-    // output axes in output order with their A / B strides
-    SimtArgs p{};
-    int64_t st0[PE_MAX_RANK], st1[PE_MAX_RANK], run = 1;
-    for (int a = pl->rank0 - 1; a >= 0; --a) { st0[a] = run; run *= pl->shape0[a]; }
-    run = 1;
-    for (int a = pl->rank1 - 1; a >= 0; --a) { st1[a] = run; run *= pl->shape1[a]; }
+int streamk_reduce_launch(const float* part, float* out, const Lowered& L, const pe_contract_plan* pl,
+                          const GemmArgs& g, cudaStream_t s) {
+    Axis ax[3 * PE_MAX_RANK];
+    int n = 0;
+    for (int j = 0; j < L.out.nb; ++j) ax[n++] = L.out.b[j];
+    for (int j = 0; j < L.out.nm; ++j) ax[n++] = L.out.m[j];
+    for (int j = 0; j < L.out.nn; ++j) ax[n++] = L.out.n[j];
+    Axis c[3 * PE_MAX_RANK];
+    int k = coalesce(ax, n, c);
+    if (k > PE_MAX_RANK) return set_last_error(PE_ERR_UNSUPPORTED);
+    Decode od = make_decode(c, k);
+    SkReduce r;
+    r.L0 = pl->L0;
+    r.L1 = pl->L1;
+    r.tm = 128;  // stream-K runs only on single-CTA 128-row tiles
+    r.bn = L.bn;
+    r.nblk = (int)((pl->L1 + r.bn - 1) / r.bn);
+    r.per_batch = ((pl->L0 + r.tm - 1) / r.tm) * (int64_t)r.nblk;
+    r.q = g.sk_q;
+    r.kiters = g.kiters;
+    const int64_t total = pl->I * pl->L0 * pl->L1;
+    int64_t blocks = (total + 255) / 256, cap = (int64_t)num_sms() * 8;
+    streamk_reduce<<<(int)std::min(blocks, cap), 256, 0, s>>>(part, out, total, r, od);
+    count_launch();
+    return check_cuda(cudaGetLastError());
+}
+
+// Output axes in output memory order with their A / B strides, and the
+// merged contraction axes: the shared setup of the streaming kernels.
+int build_simt_args(const pe_contract_plan* pl, const Lowered& L, SimtArgs& p) {
+    p = SimtArgs{};
     const int nb = L.nb, n0 = L.n0, n1 = L.n1;
     // interp axis j -> (A stride, B stride)
     int64_t ia[PE_MAX_RANK], ib[PE_MAX_RANK], isz[PE_MAX_RANK];
@@ -1157,31 +1432,52 @@ int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const vo
         p.nd++;
         n *= isz[j];
     }
-    for (int j = 0; j < L.nc; ++j) {
-        if (L.a_ct[j].size == 1) continue;
-        if (p.nk > 0 && p.ka[p.nk - 1] == L.a_ct[j].stride * L.a_ct[j].size &&
-            p.kb[p.nk - 1] == L.b_ct[j].stride * L.b_ct[j].size) {
-            p.ksize[p.nk - 1] *= L.a_ct[j].size;
-            p.ka[p.nk - 1] = L.a_ct[j].stride;
-            p.kb[p.nk - 1] = L.b_ct[j].stride;
-        } else {
-            p.ksize[p.nk] = L.a_ct[j].size;
-            p.ka[p.nk] = L.a_ct[j].stride;
-            p.kb[p.nk] = L.b_ct[j].stride;
-            p.nk++;
-        }
-    }
+    p.nk = coalesce_contraction(L, p.ksize, p.ka, p.kb);
     p.n = n;
     p.C = pl->C;
     if (n >= (1ll << 32)) return set_last_error(PE_ERR_UNSUPPORTED);
-    (void)st0;
-    (void)st1;
+    return PE_OK;
+}
+
+int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
+                          float* out, cudaStream_t s) {
+    SimtArgs p;
+    if (int rc = build_simt_args(pl, L, p)) return rc;
+    const int64_t n = p.n;
     int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms() * 8;
     const int grid = (int)std::min(blocks, cap);
     if (pl->dtype == PE_F32)
         small_contract<float><<<grid, 256, 0, s>>>((const float*)in0, (const float*)in1, out, p);
     else
         small_contract<__half><<<grid, 256, 0, s>>>((const __half*)in0, (const __half*)in1, out, p);
+    count_launch();
+    return check_cuda(cudaGetLastError());
+}
+
+int thin_contract_launch(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
+                         float* out, void* ws, cudaStream_t s) {
+    ThinArgs p;
+    if (int rc = build_simt_args(pl, L, p.s)) return rc;
+    if (p.s.nk != 1) return set_last_error(PE_ERR_INVALID);
+    p.chunk = L.thin_chunk;
+    p.nchunk = (int)L.thin_nchunk;
+    p.aligned = ((uintptr_t)in0 % 16 == 0) && ((uintptr_t)in1 % 16 == 0);
+    float* part = p.nchunk > 1 ? (float*)((uint8_t*)ws + L.p_off) : nullptr;
+    if (p.nchunk > 1 && !ws) return set_last_error(PE_ERR_WORKSPACE);
+    const int64_t warps = p.s.n * p.nchunk;
+    const int res = pl->dtype == PE_F32 ? thin_resident_blocks<float>() : thin_resident_blocks<__half>();
+    int64_t blocks = (warps + 7) / 8, cap = (int64_t)num_sms() * res;
+    const int grid = (int)std::min(blocks, cap);
+    if (pl->dtype == PE_F32)
+        thin_contract<float><<<grid, 256, 0, s>>>((const float*)in0, (const float*)in1, out, part, p);
+    else
+        thin_contract<__half><<<grid, 256, 0, s>>>((const __half*)in0, (const __half*)in1, out, part, p);
+    count_launch();
+    int rc = check_cuda(cudaGetLastError());
+    if (rc || p.nchunk == 1) return rc;
+    // partials are in output memory order
+    int64_t rb = (p.s.n + 7) / 8;
+    thin_reduce<<<(int)std::min(rb, (int64_t)num_sms() * 8), 256, 0, s>>>(part, out, p.s.n, p.nchunk);
     count_launch();
     return check_cuda(cudaGetLastError());
 }
@@ -1258,6 +1554,7 @@ int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float
 namespace {
 int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
                      float* out, void* ws, cudaStream_t s) {
+    if (L.thin) return thin_contract_launch(pl, L, in0, in1, out, ws, s);
     const int es = pl->dtype == PE_F32 ? 4 : 2;
     int rc = PE_OK;
     OperandView va = L.a, vb = L.b;
@@ -1285,6 +1582,7 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     g.ab = map_batch(va);
     g.bb = map_batch(vb);
     g.ksplit = L.ksplit;
+    g.sk_q = (int)L.sk_q;
     g.nbatch = (int)pl->I;
     g.raw_big = raw_big_enabled();
     OutView slab;  // split-K: canonical partial slabs [ksplit * I, L0, L1]
@@ -1349,7 +1647,7 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     } else {
         // pairs halve each SM's operand traffic, which pays off where the
         // mainloop dominates (long K); output-bound short-K shapes stay single
-        const bool pair = L.bn == 256 && g.K >= 512 && pairs_enabled();
+        const bool pair = L.bn == 256 && g.K >= 512 && L.sk_q == 0 && pairs_enabled();
         if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, pair ? 128 : L.bn))
             return set_last_error(PE_ERR_UNSUPPORTED);
         if (pair)
@@ -1358,6 +1656,7 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
             rc = L.bn == 256 ? launch_gemm<Cfg<256, false>>(g, s) : launch_gemm<Cfg<128, false>>(g, s);
     }
     if (rc || L.ksplit <= 1) return rc;
+    if (L.sk_q > 0) return streamk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g, s);
     return splitk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g.ksplit, s);
 }
 

@@ -69,9 +69,25 @@ SPLITK_CASES = [  # thin outputs, long contractions: split-K partials + reduce
 ]
 
 
+STREAMK_CASES = SPLITK_CASES + [  # forced stream-K on short contractions: ragged tiles,
+    ("ij, jk -> ik", (300, 1000), (1000, 200)),              # batches, permuted outputs
+    ("bij, bjk -> bik", (3, 130, 520), (3, 520, 72)),
+    ("bhsd, bhtd -> bsht", (1, 2, 128, 256), (1, 2, 128, 256)),
+    ("ki, kj -> ji", (2048, 96), (2048, 200)),
+]
+
+
+@pytest.mark.parametrize("mode", ["auto", "splitk", "streamk"])
 @pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
-@pytest.mark.parametrize("eq,s0,s1", SPLITK_CASES, ids=[case_id(*c) for c in SPLITK_CASES])
-def test_split_k(eq, s0, s1, dtype):
+@pytest.mark.parametrize("eq,s0,s1", STREAMK_CASES, ids=[case_id(*c) for c in STREAMK_CASES])
+def test_split_k(eq, s0, s1, dtype, mode, monkeypatch):
+    """Thin outputs with long contractions: split-K slabs (PE_GEMM_STREAMK=0),
+    stream-K segments (=2, forced wherever it applies) and the default choice.
+    Each must match the oracle and be bit-identical over reruns."""
+    if mode == "splitk":
+        monkeypatch.setenv("PE_GEMM_STREAMK", "0")
+    elif mode == "streamk":
+        monkeypatch.setenv("PE_GEMM_STREAMK", "2")
     b = EinsumBuilder(eq, [s0, s1], dtype)
     run = b.build()
     x, y = seeded(s0, dtype, 21, "randn"), seeded(s1, dtype, 22, "randn")
@@ -80,6 +96,63 @@ def test_split_k(eq, s0, s1, dtype):
     for _ in range(3):
         assert torch.equal(run(x.cuda(), y.cuda()), first)
     b.cleanup()
+
+
+THIN_CASES = [  # thin outputs over a contiguous contraction: warp-per-dot streaming kernel
+    ("i, i ->", (256,), (256,)), ("i, i ->", (1001,), (1001,)), ("i, i ->", (131072,), (131072,)),
+    ("ij, j -> i", (256, 4096), (4096,)), ("ij, j -> i", (3, 5000), (5000,)), ("ij, j -> i", (1000, 300), (300,)),
+    ("bij, bj -> bi", (4, 64, 4096), (4, 4096)), ("ij, kj -> ik", (96, 2048), (3, 2048)),
+    ("bhd, bhd -> bh", (8, 32, 1024), (8, 32, 1024)), ("j, ij -> i", (4104,), (7, 4104)),
+    ("ijk, ijk ->", (4, 16, 300), (4, 16, 300)),
+]
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+@pytest.mark.parametrize("eq,s0,s1", THIN_CASES, ids=[case_id(*c) for c in THIN_CASES])
+def test_thin_contraction(eq, s0, s1, dtype):
+    b = EinsumBuilder(eq, [s0, s1], dtype)
+    run = b.build()
+    x, y = seeded(s0, dtype, 51, "randn"), seeded(s1, dtype, 52, "randn")
+    first = run(x.cuda(), y.cuda()).clone()
+    r = planner.choose_operand_order("cuda", eq, s0, s1)[0]
+    if r["C"] <= 8192:
+        # the oracle sums sequentially in fp32: itself accurate only for short sums
+        check_close(first, oracle.einsum_cpu(eq, x, y), dtype)
+    # per element: |out - exact| <= 1e-6 * sum |a_i b_i| (the dot product's condition)
+    exact = torch.einsum(eq, x.double(), y.double())
+    scale = torch.einsum(eq, x.double().abs(), y.double().abs())
+    assert ((first.cpu().double() - exact).abs() <= 1e-6 * scale + 1e-30).all()
+    for _ in range(3):
+        assert torch.equal(run(x.cuda(), y.cuda()), first)
+    b.cleanup()
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=["f32", "f16"])
+def test_thin_long_dot_and_misaligned(dtype):
+    """64M-element dot product (many chunk partials) and a misaligned operand
+    base (scalar loads) against float64."""
+    n = 1 << 26
+    g = torch.Generator(device="cuda").manual_seed(61)
+    a = torch.randn(n + 1, device="cuda", generator=g).to(dtype)
+    b = torch.randn(n, device="cuda", generator=g).to(dtype)
+    for x in (a[:n], a[1:]):
+        out = einsum("i, i ->", x, b)
+        ref = (x.double() * b.double()).sum()
+        assert abs(out.item() - ref.item()) <= 1e-6 * (x.double().abs() * b.double().abs()).sum().item()
+
+
+def test_streamk_full_size_cfg4c():
+    """Config 4c ('ts,sp->tp', fp32, 8192 x 8192 x 128: 64 tiles on 148 SMs), which
+    the cost model runs as stream-K: vs float64 on the GPU."""
+    eq, s0, s1 = "ts, sp -> tp", (8192, 8192), (8192, 128)
+    g = torch.Generator(device="cuda").manual_seed(41)
+    a = torch.randn(s0, device="cuda", generator=g)
+    b = torch.randn(s1, device="cuda", generator=g)
+    out = einsum(eq, a, b)
+    ref = a.double() @ b.double()
+    err = ((out.double() - ref).norm() / ref.norm()).item()
+    assert err <= 1e-5, err
+    assert torch.equal(einsum(eq, a, b), out)
 
 
 def test_fp32_long_positive_contraction():
