@@ -345,6 +345,87 @@ def run_permute_suite(args):
                           "torch_ms": round(mt, 4)}))
 
 
+# The reference's base benchmark families (benchmarks/base/bench_einsum.py:32-178):
+# (key, equation, dtype, sizes, shapes(size)), and its transposing einsum cases
+# (benchmarks/base/bench_transpose.py:14-18).
+BASE_FAMILIES = [
+    ("matmul", "ij, jk -> ik", "float32", [128, 256, 512, 1024, 2048], lambda n: ((n, n), (n, n))),
+    ("matmul-fp16", "ij, jk -> ik", "float16", [128, 256, 512, 1024, 2048], lambda n: ((n, n), (n, n))),
+    ("transpose", "ji, jk -> ik", "float32", [128, 256, 512, 1024], lambda n: ((2 * n, n), (2 * n, n))),
+    ("outer", "i, j -> ij", "float32", [256, 512, 1024, 2048], lambda n: ((n,), (n,))),
+    ("dot-product", "i, i -> ", "float32", [4096, 16384, 49152, 131072], lambda n: ((n,), (n,))),
+    ("batch-matmul", "bij, bjk -> bik", "float32", [8, 16, 32, 64, 128], lambda b: ((b, 64, 128), (b, 128, 64))),
+    ("batch-matmul-tiny", "bij, bjk -> bik", "float32", [16, 32, 64, 128, 256],
+     lambda b: ((b, 128, 128), (b, 128, 128))),
+    ("batch-matmul-tiny-fp16", "bij, bjk -> bik", "float16", [16, 32, 64, 128, 256],
+     lambda b: ((b, 128, 128), (b, 128, 128))),
+    ("contraction", "ijk, jkl -> il", "float32", [32, 64, 128, 256], lambda k: ((64, 64, k), (64, k, 64))),
+    ("custom-layout", "abc, cd -> abd", "float32", [8, 16, 32, 64], lambda a: ((a, 64, 128), (128, 256))),
+    ("gdn-kkt-nt", "bihd, bjhd -> bihj", "float32", [8, 16, 32, 64],
+     lambda b: ((b, 128, 16, 128), (b, 128, 16, 128))),
+    ("gdn-wy-fast-nn", "bihj, bjhd -> bihd", "float32", [8, 16, 32, 64],
+     lambda b: ((b, 128, 16, 128), (b, 128, 16, 128))),
+    ("gdn-chunk-h-tn", "bvhd, bvhe -> bhde", "float32", [8, 16, 32, 64],
+     lambda b: ((b, 128, 16, 128), (b, 128, 16, 128))),
+    ("unaligned", "ij, jk -> ik", "float32", [128, 256, 512, 1024], lambda n: ((n, n - 6), (n - 6, n))),
+    ("batch-unaligned", "bij, bjk -> bik", "float32", [8, 16, 32, 64], lambda b: ((b, 64, 100), (b, 100, 64))),
+    ("transpose-2d", "ai, ja -> ij", "float32", [64, 256, 512], lambda n: ((n, n), (n, n))),
+]
+
+
+def run_base_suite(args):
+    """The reference's base benchmark sweep on one B200: per point the build time,
+    the median host wall time of one call followed by a synchronize (the reference's
+    own method, bench_einsum.py:183-215) for this library and torch.einsum, the
+    device time per call of back-to-back calls (CUDA events), and the relative
+    Frobenius error against float64. Inputs U[0,1) as in the reference."""
+    from pto_einsum import EinsumBuilder
+    dev = torch.device("cuda", 0)
+    runs = max(args.steps // 2, 20)
+    for key, eq, dts, sizes, make in BASE_FAMILIES:
+        dt = getattr(torch, dts)
+        for n in sizes:
+            s0, s1 = make(n)
+            a = torch.rand(s0, device=dev).to(dt)
+            b = torch.rand(s1, device=dev).to(dt)
+            row = {"suite": "base", "family": key, "equation": eq, "dtype": dts, "size": n,
+                   "shape0": list(s0), "shape1": list(s1)}
+            t0 = time.perf_counter()
+            try:
+                bld = EinsumBuilder(eq, [s0, s1], dt)
+                run = bld.build()
+            except ValueError as e:
+                row["unsupported"] = str(e)[:120]
+                print(json.dumps(row))
+                continue
+            row["build_s"] = round(time.perf_counter() - t0, 3)
+
+            def wall(fn):
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize()
+                ts = []
+                for _ in range(runs):
+                    t = time.perf_counter()
+                    fn()
+                    torch.cuda.synchronize()
+                    ts.append((time.perf_counter() - t) * 1e3)
+                return statistics.median(ts)
+            ours = lambda: run(a, b)  # noqa: E731
+            theirs = lambda: torch.einsum(eq, a, b)  # noqa: E731
+            row["ms"] = round(wall(ours), 4)
+            row["torch_ms"] = round(wall(theirs), 4)
+            row["speedup"] = round(row["torch_ms"] / row["ms"], 3)
+            row["device_us"] = round(_time(ours, runs, 3) * 1e3, 2)
+            row["torch_device_us"] = round(_time(theirs, runs, 3) * 1e3, 2)
+            exact = torch.einsum(eq, a.double(), b.double())
+            got = run(a, b).double()
+            den = exact.norm().item()
+            row["rel_err"] = float(((got - exact).norm() / den).item()) if den else 0.0
+            bld.cleanup()
+            print(json.dumps(row), flush=True)
+
+
 def run_gdn_suite(args):
     """GDN stage backends (the reference's benchmarks/complex/gdn/bench_gdn_4way.py
     workloads: N_seq x L_seg in {1,2} x {512,1024}, H=32 value heads, Hg=16 key heads,
@@ -424,7 +505,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=6)
-    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base"],
                     help="instead of the one-line benchmark: time the LLM contraction patterns and the "
                          "linear-attention chain against torch.einsum (one JSON line per op)")
     ap.add_argument("--shrink", type=int, default=1,
@@ -453,6 +534,9 @@ def main():
         return
     if args.suite == "gdn":
         run_gdn_suite(args)
+        return
+    if args.suite == "base":
+        run_base_suite(args)
         return
 
     dist = None

@@ -1235,7 +1235,9 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
     // contraction, e.g. a broadcast planned as 262144 batches of 4x1x1) would
     // fill a 128-row MMA tile with almost nothing; they run on the streaming
     // kernel and need no scratch.
-    L->simt = std::min(L0, L1) <= 4 && C <= 64;
+    // Contractions of at most 4 elements (outer products and the like) are a
+    // pure output stream; the MMA path would pad K to a full k-step.
+    L->simt = (std::min(L0, L1) <= 4 && C <= 64) || C <= 4;
     if (L->simt) {
         L->a_ws = L->b_ws = false;
         L->ws_bytes = 0;
@@ -1302,13 +1304,16 @@ int lower(const pe_contract_plan* pl, const void* in0, const void* in1, Lowered*
     // by several CTAs gets one partial per CTA boundary inside it.
     // PE_GEMM_STREAMK=0 disables it, =2 forces it wherever it can apply.
     const int skm = streamk_mode();
-    if (skm && tiles > 0 && tiles < nsm && kiters >= (skm == 2 ? 2 : 64)) {
+    if (skm && tiles > 0 && tiles < nsm && kiters >= (skm == 2 ? 2 : 16)) {
         const int64_t total = tiles * kiters;
         const int64_t ncta = std::min<int64_t>(nsm, total / (skm == 2 ? 2 : 8));
         if (ncta > tiles) {
             const int64_t q = (total + ncta - 1) / ncta;
             const double segs = (double)(tiles + ncta - 1) / (double)tiles;
-            const double cost = (double)q / (double)kiters + segs * part_bytes / in_bytes;
+            // partial slabs that stay in L2 (small problems) cost far less than
+            // their HBM bytes suggest
+            const double l2_scale = (in_bytes + segs * part_bytes) < 48.0 * (1 << 20) ? 0.2 : 1.0;
+            const double cost = (double)q / (double)kiters + l2_scale * segs * part_bytes / in_bytes;
             if (skm == 2 || cost < best - 0.02) {
                 best = cost;
                 L->sk_q = q;
@@ -1435,7 +1440,8 @@ int build_simt_args(const pe_contract_plan* pl, const Lowered& L, SimtArgs& p) {
     p.nk = coalesce_contraction(L, p.ksize, p.ka, p.kb);
     p.n = n;
     p.C = pl->C;
-    if (n >= (1ll << 32)) return set_last_error(PE_ERR_UNSUPPORTED);
+    // 32-bit element indices and grid strides in the streaming kernels
+    if (n >= (1ll << 31)) return set_last_error(PE_ERR_UNSUPPORTED);
     return PE_OK;
 }
 
@@ -1444,8 +1450,9 @@ int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const vo
     SimtArgs p;
     if (int rc = build_simt_args(pl, L, p)) return rc;
     const int64_t n = p.n;
-    int64_t blocks = (n + 255) / 256, cap = (int64_t)num_sms() * 8;
-    const int grid = (int)std::min(blocks, cap);
+    // one output element per thread (n < 2^31): every element's operand loads
+    // are in flight at once instead of a latency-bound walk per thread
+    const int grid = (int)((n + 255) / 256);
     if (pl->dtype == PE_F32)
         small_contract<float><<<grid, 256, 0, s>>>((const float*)in0, (const float*)in1, out, p);
     else

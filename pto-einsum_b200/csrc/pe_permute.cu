@@ -237,7 +237,7 @@ int launch_copy(const void* src, void* dst, const CopyParams& cp, cudaStream_t s
     const int last = cp.nd - 1;
     // (1) innermost axis unit-stride on both sides: vectorised run copy
     if (al && cp.nd >= 1 && cp.sst[last] == 1 && cp.dst[last] == 1 && cp.size[last] % VEC == 0 &&
-        cp.n / VEC < (1ll << 32)) {
+        cp.n / VEC < (1ll << 31)) {
         bool ok = true;
         RunParams rp{};
         rp.nd = cp.nd - 1;
