@@ -60,8 +60,16 @@ class EinsumBuilder:
     """Plan, compile (with caching) and run one two-operand einsum on a B200."""
 
     def __init__(self, equation: str, input_shapes: Sequence[Sequence[int]], dtype: torch.dtype,
-                 device="cuda"):
+                 device="cuda", extended: bool = False):
+        """``extended=False`` plans exactly as the reference. ``extended=True`` lifts
+        two of the reference's roadmap gaps (IMPLEMENTATION.md "Roadmap"): broadcasts
+        whose inner run exceeds its tile cap stay broadcasts instead of taking the
+        matmul route, and single-operand reduction axes (``ij,jk->k``), which the
+        reference rejects, are summed by a first contraction of the owning operand
+        with a ones vector; the remaining einsum then runs in fp32."""
         self.equation = equation
+        self.extended = extended
+        self._composite = None          # (pre-reductions, main builder) for solo axes
         self.input_shapes = input_shapes
         self.dtype = dtype
         self.device = device
@@ -115,12 +123,75 @@ class EinsumBuilder:
         if len(self.input_shapes) != 2:
             raise ValueError("Only exactly two input shapes are supported.")
         shape0, shape1 = (tuple(int(d) for d in s) for s in self.input_shapes)
+        if self.extended and self._plan_solo_reductions(shape0, shape1):
+            return
         self.recipe, self._swap_operands = planner.choose_operand_order(
-            self._plan_device, self.equation, shape0, shape1)
+            self._plan_device, self.equation, shape0, shape1, self.extended)
         self._exec_shapes = (shape1, shape0) if self._swap_operands else (shape0, shape1)
         r = self.recipe
         if not r['elementwise'] and not r['broadcast']:
             self._axes = planner.axis_groups(self.equation, r, self._swap_operands)
+
+    def _plan_solo_reductions(self, shape0, shape1) -> bool:
+        """Split an equation with single-operand reduction axes into per-operand
+        pre-contractions with ones vectors plus the remaining two-operand einsum.
+        Returns False when the equation has no such axes."""
+        solo = planner.solo_reductions(self.equation)
+        if not solo[0] and not solo[1]:
+            return False
+        planner.validate_expr(self.equation, shape0, shape1)
+        a, b, o = planner.split_equation(self.equation.replace(" ", ""))
+        pre = []
+        labels, shapes = [], []
+        for k, (lab, shp, sol) in enumerate(((a, shape0, solo[0]), (b, shape1, solo[1]))):
+            kept = "".join(ch for ch in lab if ch not in sol)
+            if sol:
+                if not kept:
+                    raise ValueError(f"einsum '{self.equation}': operand {k} is reduced to a scalar; "
+                                     "at least one of its indices must remain")
+                ones_shape = tuple(shp[lab.index(ch)] for ch in sol)
+                sub = EinsumBuilder(f"{lab},{''.join(sol)}->{kept}", [shp, ones_shape], self.dtype,
+                                    device=self.device)
+                sub.parse_equation()
+                pre.append((k, sub, ones_shape))
+                shp = tuple(shp[lab.index(ch)] for ch in kept)
+            labels.append(kept)
+            shapes.append(tuple(shp))
+        main = EinsumBuilder(f"{labels[0]},{labels[1]}->{o}", shapes, torch.float32, device=self.device,
+                             extended=True)
+        main.parse_equation()
+        self._composite = (pre, main)
+        self.recipe = main.recipe
+        self._swap_operands = False
+        return True
+
+    def _build_composite(self):
+        pre, main = self._composite
+        runs = [(k, sub.build(), ones_shape) for k, sub, ones_shape in pre]
+        main_run = main.build()
+        ones = {}
+        shapes = (tuple(self.input_shapes[0]), tuple(self.input_shapes[1]))
+
+        def run(*operands):
+            if len(operands) != 2:
+                raise ValueError("Expected exactly two operands.")
+            ops = list(operands)
+            for k in (0, 1):
+                if tuple(ops[k].shape) != shapes[k]:
+                    raise ValueError(f"Input shapes {ops[0].shape} and {ops[1].shape} do not match built "
+                                     f"shapes {self.input_shapes}.")
+                if ops[k].dtype != self.dtype:
+                    raise TypeError(f"Input datatypes {ops[0].dtype} and {ops[1].dtype} do not match built "
+                                    f"datatype {self.dtype}.")
+            for k, sub_run, ones_shape in runs:
+                key = (k, ops[k].device)
+                if key not in ones:
+                    ones[key] = torch.ones(ones_shape, dtype=self.dtype, device=ops[k].device)
+                ops[k] = sub_run(ops[k], ones[key])
+            ops = [x if x.dtype == torch.float32 else x.float() for x in ops]
+            return main_run(ops[0], ops[1])
+
+        return run
 
     def einsum_config_gen(self, tpose_inp0_name, tpose_inp1_name, tpose_out_name):
         r = self.recipe
@@ -263,6 +334,8 @@ class EinsumBuilder:
 
     def build(self):
         self.parse_equation()
+        if self._composite is not None:
+            return self._build_composite()
         self.generate_code()
         self.compile()
         self.load_library()
@@ -334,18 +407,24 @@ class EinsumBuilder:
             pass
 
     def cleanup(self):
+        if self._composite is not None:
+            for _, sub, _ in self._composite[0]:
+                sub.cleanup()
+            self._composite[1].cleanup()
         self._free_workspaces()
         self.lib = None
         if self.target_dir and os.path.exists(self.target_dir):
             shutil.rmtree(self.target_dir)
 
 
-def einsum(equation: str, *operands, device="cuda"):
-    """One-shot two-operand einsum on CUDA; returns an fp32 tensor (builder.py:887-902)."""
+def einsum(equation: str, *operands, device="cuda", extended: bool = False):
+    """One-shot two-operand einsum on CUDA; returns an fp32 tensor (builder.py:887-902).
+    ``extended`` as in EinsumBuilder."""
     if len(operands) != 2:
         raise ValueError("Only exactly two operands are supported.")
     inp0, inp1 = operands
     if inp0.dtype != inp1.dtype:
         raise ValueError("Operands must have the same datatype.")
-    runner = EinsumBuilder(equation, [inp0.shape, inp1.shape], inp0.dtype, device=device).build()
+    runner = EinsumBuilder(equation, [inp0.shape, inp1.shape], inp0.dtype, device=device,
+                           extended=extended).build()
     return runner(inp0, inp1)

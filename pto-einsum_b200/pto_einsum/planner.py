@@ -149,12 +149,16 @@ def validate_expr(fn: str, shape0: Sequence[int], shape1: Sequence[int]):
     return f'{in0},{in1}->{out}', out_shape
 
 
-def try_broadcast(device: str, in0, in1, out, shape0, shape1, out_shape) -> Optional[EinsumRecipe]:
+def try_broadcast(device: str, in0, in1, out, shape0, shape1, out_shape,
+                  extended: bool = False) -> Optional[EinsumRecipe]:
     """Classify a contraction-free equation as a broadcast multiply, else None.
 
     Mode 0 ("ColExpand"): the broadcast operand B varies along the innermost
     output run; mode 1 ("scalar"): B is constant over the innermost block.
     Follows ``builder.py:369-447``; the CPU device never takes this route.
+    ``extended`` drops the reference's tile caps (an inner run above
+    BCAST_TILECAP, a scalar-mode operand above BCAST_SCALAR_SIZE_CAP), which it
+    sends down the matmul route instead: the CUDA broadcast kernels take any size.
     """
     if device == "cpu":
         return None
@@ -186,7 +190,7 @@ def try_broadcast(device: str, in0, in1, out, shape0, shape1, out_shape) -> Opti
         mode = 0
         cc = 1
         while p >= 0 and in_b[p]:
-            if cc * sizes[p] > BCAST_TILECAP:
+            if cc * sizes[p] > BCAST_TILECAP and not extended:
                 return None
             cc *= sizes[p]
             p -= 1
@@ -197,7 +201,7 @@ def try_broadcast(device: str, in0, in1, out, shape0, shape1, out_shape) -> Opti
         inner = rr * cc
     else:
         mode = 1
-        if size_b > BCAST_SCALAR_SIZE_CAP:
+        if size_b > BCAST_SCALAR_SIZE_CAP and not extended:
             return None
         inner = 1
         while p >= 0 and not in_b[p]:
@@ -224,8 +228,10 @@ def try_broadcast(device: str, in0, in1, out, shape0, shape1, out_shape) -> Opti
     return EinsumRecipe(**recipe)
 
 
-def parse_recipe(device: str, fn: str, shape0: Sequence[int], shape1: Sequence[int]) -> EinsumRecipe:
-    """Build the plan for one operand order (``builder.py:185-367``)."""
+def parse_recipe(device: str, fn: str, shape0: Sequence[int], shape1: Sequence[int],
+                 extended: bool = False) -> EinsumRecipe:
+    """Build the plan for one operand order (``builder.py:185-367``); ``extended``
+    lifts the broadcast caps (see try_broadcast)."""
     fn, out_shape = validate_expr(fn, shape0, shape1)
     s0, s1, so = split_equation(fn)
     in0, in1, out = list(s0), list(s1), list(so)
@@ -257,7 +263,7 @@ def parse_recipe(device: str, fn: str, shape0: Sequence[int], shape1: Sequence[i
             "is reduced away; single-operand reduction is not supported.")
 
     if not contracted:
-        bc = try_broadcast(device, in0, in1, out, shape0, shape1, out_shape)
+        bc = try_broadcast(device, in0, in1, out, shape0, shape1, out_shape, extended)
         if bc is not None:
             return bc
 
@@ -352,19 +358,19 @@ def is_identity(perm: Sequence[int]) -> bool:
     return tuple(perm) == tuple(range(len(perm)))
 
 
-def choose_operand_order(device: str, equation: str, shape0, shape1):
+def choose_operand_order(device: str, equation: str, shape0, shape1, extended: bool = False):
     """Plan the equation, swapping the operands when that removes an output permute.
 
     Returns ``(recipe, swapped)``. The swap is adopted only when the natural
     order keeps a non-fusible, non-identity output and the swapped order makes
     it fusible or identity (``builder.py:562-586``).
     """
-    recipe = parse_recipe(device, equation, shape0, shape1)
+    recipe = parse_recipe(device, equation, shape0, shape1, extended)
     is_mm = not recipe['elementwise'] and not recipe['broadcast']
     if (os.getenv("EINSUM_DISABLE_OPERAND_SWAP", "0") == "0" and is_mm
             and not recipe['out_fusible'] and not is_identity(recipe['out_transpose_idxs'])):
         a, b, o = split_equation(equation)
-        alt = parse_recipe(device, f"{b},{a}->{o}", shape1, shape0)
+        alt = parse_recipe(device, f"{b},{a}->{o}", shape1, shape0, extended)
         if alt['out_fusible'] or is_identity(alt['out_transpose_idxs']):
             return alt, True
     return recipe, False
@@ -448,3 +454,16 @@ def axis_groups(equation: str, recipe: EinsumRecipe, swapped: bool) -> Tuple[int
     n0 = len((so - (sa & sb)) & sa)
     n1 = len((so - (sa & sb)) & sb)
     return nb, n0, n1, nc
+
+
+def solo_reductions(equation: str):
+    """Single-operand reduction labels: (labels only in operand 0 and not in the
+    output, same for operand 1). The reference rejects such equations
+    (``builder.py:185-367`` via the check above); ``EinsumBuilder(extended=True)``
+    computes them by first contracting the owning operand with a ones vector
+    over those labels."""
+    a, b, o = split_equation(equation.replace(" ", ""))
+    sa, sb, so = set(a), set(b), set(o)
+    solo0 = [ch for ch in a if ch not in sb and ch not in so]
+    solo1 = [ch for ch in b if ch not in sa and ch not in so]
+    return solo0, solo1
