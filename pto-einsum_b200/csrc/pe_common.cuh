@@ -105,14 +105,6 @@ __device__ __forceinline__ void tma_prefetch(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
-// L2 prefetch of a 5-D tile (no shared memory, no completion): warms L2 so the
-// later TMA load of the same box hits it.
-__device__ __forceinline__ void tma_prefetch_l2_5d(const void* tmap, int c0, int c1, int c2, int c3, int c4) {
-    asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(tmap),
-                 "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-                 : "memory");
-}
-
 // 5-D tiled load into CTA shared memory, completion signalled on `bar`.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
                                             int c1, int c2, int c3, int c4) {

@@ -67,7 +67,6 @@ struct GemmArgs {
     int ksplit;      // work units per output tile (split-K), >= 1
     int kper;        // k-iterations per unit
     int sk_q;        // stream-K: k-iterations per CTA (group) over the flattened (tile, k) space; 0 = off
-    int l2pf;        // K-major A: prefetch the next k-step's A box into L2 with each load
     int nbatch;      // I: batch count of the plan (split-K partials use batch i + sp*I)
     int raw_big;     // fp32: feed x unmasked as the big part (tensor core truncation)
     float* out;
@@ -288,10 +287,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     };
                     load_a(sa, &g.tma);
                     load_b(sb, &g.tmb);
-                    // the neighbouring 128 bytes of the same A rows, requested now so
-                    // DRAM serves them from the rows it just opened
-                    if (g.l2pf && !g.a_mn && kb + 1 < kb_hi)
-                        tma_prefetch_l2_5d(&g.tma, k0 + C::BK, m0, ca[0], ca[1], ca[2]);
                     if constexpr (C::F32) {
                         if (g.a_pre) load_a(sa + C::TX_BYTES, &g.tmas);
                         if (g.b_pre) load_b(sb + C::TX_BYTES, &g.tmbs);
@@ -843,11 +838,6 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
 int wide_fp32_enabled() {
     const char* e = getenv("PE_GEMM_WIDE_FP32");
     return (e && e[0] == '0') ? 0 : 1;
-}
-
-int l2pf_enabled() {
-    const char* e = getenv("PE_GEMM_L2PF");
-    return (e && e[0] == '1') ? 1 : 0;
 }
 
 int thin_enabled() {
@@ -1600,7 +1590,6 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     g.bb = map_batch(vb);
     g.ksplit = L.ksplit;
     g.sk_q = (int)L.sk_q;
-    g.l2pf = l2pf_enabled();
     g.nbatch = (int)pl->I;
     g.raw_big = raw_big_enabled();
     OutView slab;  // split-K: canonical partial slabs [ksplit * I, L0, L1]
