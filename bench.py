@@ -504,7 +504,8 @@ def main():
     ap.add_argument("--config", default="cfg2", choices=sorted(CFG))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=16,
+                    help="pipelined end-to-end steps (fill and drain cost about one step)")
     ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base"],
                     help="instead of the one-line benchmark: time the LLM contraction patterns and the "
                          "linear-attention chain against torch.einsum (one JSON line per op)")
