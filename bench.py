@@ -345,6 +345,50 @@ def run_permute_suite(args):
                           "torch_ms": round(mt, 4)}))
 
 
+def run_thin_suite(args):
+    """Thin outputs and few-tile long contractions: dot and matrix-vector products
+    (streaming thin-output kernel) and thin GEMMs (stream-K), each vs torch.einsum,
+    with the relative Frobenius error against float64. For the GEMM cases the same
+    call with stream-K disabled (PE_GEMM_STREAMK=0, split-K only) is timed too."""
+    from pto_einsum import EinsumBuilder
+    dev = torch.device("cuda", 0)
+    steps = max(args.steps // 10, 10)
+    cases = [("i, i ->", (1 << 26,), (1 << 26,)), ("ij, j -> i", (256, 1 << 18), (1 << 18,)),
+             ("bhd, bhd -> bh", (16, 32, 1 << 14), (16, 32, 1 << 14)),
+             ("ij, jk -> ik", (128, 1 << 20), (1 << 20, 128)), ("ts, sp -> tp", (8192, 8192), (8192, 128))]
+    for dt in (torch.float32, torch.float16):
+        for eq, s0, s1 in cases:
+            g = torch.Generator(device=dev).manual_seed(7)
+            a = torch.randn(s0, device=dev, generator=g).to(dt)
+            b = torch.randn(s1, device=dev, generator=g).to(dt)
+            exact = torch.einsum(eq, a.double(), b.double())
+            row = {"suite": "thin", "equation": eq, "shape0": list(s0), "shape1": list(s1),
+                   "dtype": str(dt).split(".")[-1]}
+            nbytes = (a.numel() + b.numel()) * a.element_size()
+            modes = [("", None)] + ([("splitk_", "0")] if "k" in eq.split("->")[0] else [])
+            for tag, env in modes:
+                old = os.environ.get("PE_GEMM_STREAMK")
+                if env is not None:
+                    os.environ["PE_GEMM_STREAMK"] = env
+                try:
+                    bld = EinsumBuilder(eq, [s0, s1], dt)
+                    run = bld.build()
+                    ms = _time(lambda: run(a, b), steps, 3)
+                    out = run(a, b).double()
+                    bld.cleanup()
+                finally:
+                    if env is not None:
+                        if old is None:
+                            os.environ.pop("PE_GEMM_STREAMK", None)
+                        else:
+                            os.environ["PE_GEMM_STREAMK"] = old
+                row[f"{tag}us"] = round(ms * 1e3, 1)
+                row[f"{tag}rel_err"] = float(((out - exact).norm() / exact.norm()).item())
+            row["input_GB/s"] = round(nbytes / (row["us"] * 1e-6) / 1e9, 1)
+            row["torch_us"] = round(_time(lambda: torch.einsum(eq, a, b), steps, 3) * 1e3, 1)
+            print(json.dumps(row), flush=True)
+
+
 # The reference's base benchmark families (benchmarks/base/bench_einsum.py:32-178):
 # (key, equation, dtype, sizes, shapes(size)), and its transposing einsum cases
 # (benchmarks/base/bench_transpose.py:14-18).
@@ -506,7 +550,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16,
                     help="pipelined end-to-end steps (fill and drain cost about one step)")
-    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin"],
                     help="instead of the one-line benchmark: time the LLM contraction patterns and the "
                          "linear-attention chain against torch.einsum (one JSON line per op)")
     ap.add_argument("--shrink", type=int, default=1,
@@ -538,6 +582,9 @@ def main():
         return
     if args.suite == "base":
         run_base_suite(args)
+        return
+    if args.suite == "thin":
+        run_thin_suite(args)
         return
 
     dist = None

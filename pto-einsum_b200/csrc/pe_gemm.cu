@@ -1007,6 +1007,33 @@ __global__ void __launch_bounds__(256) thin_reduce(const float* __restrict__ par
     }
 }
 
+// Many partials per output (dot products): a 256-thread block per output;
+// thread k sums partials k, k + 256, ... with four accumulators in a fixed
+// pattern, then a fixed shared-memory tree (run-to-run identical).
+__global__ void __launch_bounds__(256) thin_reduce_block(const float* __restrict__ part, float* __restrict__ out,
+                                                         int64_t n, int nchunk) {
+    __shared__ float red[256];
+    for (int64_t e = blockIdx.x; e < n; e += gridDim.x) {
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int j = threadIdx.x;
+        for (; j + 768 < nchunk; j += 1024) {
+            a0 += part[(int64_t)j * n + e];
+            a1 += part[(int64_t)(j + 256) * n + e];
+            a2 += part[(int64_t)(j + 512) * n + e];
+            a3 += part[(int64_t)(j + 768) * n + e];
+        }
+        for (; j < nchunk; j += 256) a0 += part[(int64_t)j * n + e];
+        red[threadIdx.x] = (a0 + a1) + (a2 + a3);
+        __syncthreads();
+        for (int w = 128; w > 0; w >>= 1) {
+            if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) out[e] = red[0];
+        __syncthreads();
+    }
+}
+
 template <typename T>
 int thin_resident_blocks() {
     static int n = 0;
@@ -1483,8 +1510,13 @@ int thin_contract_launch(const pe_contract_plan* pl, const Lowered& L, const voi
     int rc = check_cuda(cudaGetLastError());
     if (rc || p.nchunk == 1) return rc;
     // partials are in output memory order
-    int64_t rb = (p.s.n + 7) / 8;
-    thin_reduce<<<(int)std::min(rb, (int64_t)num_sms() * 8), 256, 0, s>>>(part, out, p.s.n, p.nchunk);
+    if (p.nchunk >= 1024) {
+        thin_reduce_block<<<(int)std::min(p.s.n, (int64_t)num_sms() * 8), 256, 0, s>>>(part, out, p.s.n,
+                                                                                      p.nchunk);
+    } else {
+        int64_t rb = (p.s.n + 7) / 8;
+        thin_reduce<<<(int)std::min(rb, (int64_t)num_sms() * 8), 256, 0, s>>>(part, out, p.s.n, p.nchunk);
+    }
     count_launch();
     return check_cuda(cudaGetLastError());
 }
