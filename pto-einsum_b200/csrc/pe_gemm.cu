@@ -874,6 +874,53 @@ struct SimtArgs {
     int64_t n, C;
 };
 
+// Four consecutive outputs along the innermost output axis per thread (its size
+// a multiple of 4, output 16-byte aligned): one index decode and one 16-byte
+// store per four elements; the same single-rounded products and sums as
+// small_contract, so results are identical.
+template <typename T>
+__global__ void __launch_bounds__(256) small_contract4(const T* __restrict__ A, const T* __restrict__ B,
+                                                       float* __restrict__ out, SimtArgs p) {
+    const uint32_t n4 = (uint32_t)(p.n >> 2);
+    const uint32_t step = gridDim.x * blockDim.x;
+    const int64_t ia = p.sa[p.nd - 1], ib = p.sb[p.nd - 1];
+    for (uint32_t e4 = blockIdx.x * blockDim.x + threadIdx.x; e4 < n4; e4 += step) {
+        uint32_t rem = e4 << 2;
+        int64_t ao = 0, bo = 0;
+        for (int a = p.nd - 1; a >= 0; --a) {
+            const uint32_t q = fdiv(rem, p.div[a]);
+            const uint32_t idx = rem - q * p.div[a].div;
+            rem = q;
+            ao += (int64_t)idx * p.sa[a];
+            bo += (int64_t)idx * p.sb[a];
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (p.nk <= 1) {
+            const int64_t ka = p.nk ? p.ka[0] : 0, kb = p.nk ? p.kb[0] : 0;
+            for (int64_t c = 0; c < p.C; ++c) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    acc[q] = __fadd_rn(acc[q], __fmul_rn((float)A[ao + q * ia + c * ka], (float)B[bo + q * ib + c * kb]));
+            }
+        } else {
+            for (int64_t c = 0; c < p.C; ++c) {
+                int64_t r = c, oa = ao, ob = bo;
+                for (int a = p.nk - 1; a >= 0; --a) {
+                    const int64_t q = r / p.ksize[a];
+                    const int64_t idx = r - q * p.ksize[a];
+                    r = q;
+                    oa += idx * p.ka[a];
+                    ob += idx * p.kb[a];
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    acc[q] = __fadd_rn(acc[q], __fmul_rn((float)A[oa + q * ia], (float)B[ob + q * ib]));
+            }
+        }
+        *reinterpret_cast<float4*>(out + ((int64_t)e4 << 2)) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) small_contract(const T* __restrict__ A, const T* __restrict__ B,
                                                       float* __restrict__ out, SimtArgs p) {
@@ -1477,6 +1524,16 @@ int small_contract_launch(const pe_contract_plan* pl, const Lowered& L, const vo
     SimtArgs p;
     if (int rc = build_simt_args(pl, L, p)) return rc;
     const int64_t n = p.n;
+    // four outputs per thread where the innermost output axis allows it
+    if (p.nd >= 1 && p.div[p.nd - 1].div % 4 == 0 && ((uintptr_t)out & 15) == 0) {
+        const int grid4 = (int)((n / 4 + 255) / 256);
+        if (pl->dtype == PE_F32)
+            small_contract4<float><<<grid4, 256, 0, s>>>((const float*)in0, (const float*)in1, out, p);
+        else
+            small_contract4<__half><<<grid4, 256, 0, s>>>((const __half*)in0, (const __half*)in1, out, p);
+        count_launch();
+        return check_cuda(cudaGetLastError());
+    }
     // one output element per thread (n < 2^31): every element's operand loads
     // are in flight at once instead of a latency-bound walk per thread
     const int grid = (int)((n + 255) / 256);
