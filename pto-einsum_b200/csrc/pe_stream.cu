@@ -99,21 +99,23 @@ __global__ void __launch_bounds__(256) ew_mul_f16_vec(const uint4* __restrict__ 
     const int lane = threadIdx.x & 31;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t step = (int64_t)gridDim.x * blockDim.x;
-    for (; i < nvec; i += 2 * step) {
-        const int64_t i1 = i + step;
-        const bool two = i1 < nvec;
-        const uint4 a0 = ld_stream(a + i), b0 = ld_stream(b + i);
-        uint4 a1 = make_uint4(0, 0, 0, 0), b1 = a1;
-        if (two) {
-            a1 = ld_stream(a + i1);
-            b1 = ld_stream(b + i1);
+    // four vectors of each operand in flight per thread
+    for (; i < nvec; i += 4 * step) {
+        uint4 x[4], y[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int64_t iq = i + q * step;
+            x[q] = iq < nvec ? ld_stream(a + iq) : make_uint4(0, 0, 0, 0);
+            y[q] = iq < nvec ? ld_stream(b + iq) : make_uint4(0, 0, 0, 0);
         }
-        float p[8];
-        mul8(a0, b0, p);
-        store8(out, i, lane, i - lane + 32 <= nvec, p);
-        if (two) {
-            mul8(a1, b1, p);
-            store8(out, i1, lane, i1 - lane + 32 <= nvec, p);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int64_t iq = i + q * step;
+            if (iq < nvec) {
+                float p[8];
+                mul8(x[q], y[q], p);
+                store8(out, iq, lane, iq - lane + 32 <= nvec, p);
+            }
         }
     }
 }
@@ -189,8 +191,8 @@ __device__ __forceinline__ void bcast_apply(const T* __restrict__ bc, float* __r
 
 // Vector path: Inner and Cc are multiples of VEC, so a vector never crosses a
 // group and (mode 0) the matching broadcast run is VEC contiguous elements.
-// Each iteration issues two independent 16-byte loads of the full operand
-// before using either, to keep more bytes in flight per thread.
+// Each iteration issues four independent 16-byte loads of the full operand
+// before using any, to keep more bytes in flight per thread.
 template <typename T>
 __global__ void __launch_bounds__(256) bcast_mul_vec(const T* __restrict__ full,
                                                      const T* __restrict__ bc,
@@ -200,13 +202,18 @@ __global__ void __launch_bounds__(256) bcast_mul_vec(const T* __restrict__ full,
     const uint32_t nvec = (uint32_t)(p.n / VEC);
     const uint32_t step = gridDim.x * blockDim.x;
     const uint4* src = reinterpret_cast<const uint4*>(full);
-    for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 2 * step) {
-        const uint32_t v1 = v + step;
-        const uint4 a0 = ld_stream(src + v);
-        uint4 a1 = make_uint4(0, 0, 0, 0);
-        if (v1 < nvec) a1 = ld_stream(src + v1);
-        bcast_apply<T>(bc, out, p, v, a0, lane, (int64_t)v - lane + 32 <= (int64_t)nvec);
-        if (v1 < nvec) bcast_apply<T>(bc, out, p, v1, a1, lane, (int64_t)v1 - lane + 32 <= (int64_t)nvec);
+    for (uint32_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += 4 * step) {
+        uint4 a[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t vq = v + q * step;
+            a[q] = vq < nvec ? ld_stream(src + vq) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t vq = v + q * step;
+            if (vq < nvec) bcast_apply<T>(bc, out, p, vq, a[q], lane, (int64_t)vq - lane + 32 <= (int64_t)nvec);
+        }
     }
 }
 
@@ -257,7 +264,7 @@ int elementwise_mul(int32_t dtype, const void* a, const void* b, float* out, int
             ew_mul_f32_vec<<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>(
                 (const float4*)a, (const float4*)b, (float4*)out, nvec);
         else
-            ew_mul_f16_vec<<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const uint4*)a, (const uint4*)b,
+            ew_mul_f16_vec<<<grid_for((nvec + 3) / 4, 256), 256, 0, s>>>((const uint4*)a, (const uint4*)b,
                                                                          out, nvec);
         count_launch();
     }
@@ -306,10 +313,10 @@ int broadcast_mul(const pe_broadcast_plan* pl, const void* full, const void* bc,
         }
         int64_t nvec = pl->n / vec;
         if (pl->dtype == PE_F32)
-            bcast_mul_vec<float><<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const float*)full,
+            bcast_mul_vec<float><<<grid_for((nvec + 3) / 4, 256), 256, 0, s>>>((const float*)full,
                                                                     (const float*)bc, out, p);
         else
-            bcast_mul_vec<__half><<<grid_for((nvec + 1) / 2, 256), 256, 0, s>>>((const __half*)full,
+            bcast_mul_vec<__half><<<grid_for((nvec + 3) / 4, 256), 256, 0, s>>>((const __half*)full,
                                                                      (const __half*)bc, out, p);
     } else {
         BcastGeneric p{};
