@@ -1,18 +1,24 @@
 #!/usr/bin/env python
 """Benchmark of the B200 einsum hot path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2] [--configs all|none|a,b]
+                    [--impl ours|reference] [--suite callers|permute|gdn|base|thin]
 
-A step is one einsum call (one fused launch on the contraction routes) over
-one full BASELINE config, inputs resident in HBM. Under torchrun each rank
-runs its own full-size shard of the batch axis (weak scaling: global batch =
-N x config batch); there is no collective on the data path. Timing: CUDA
-events on the launching stream around exactly K steps, bracketed by a
-barrier and torch.cuda.synchronize(), max over ranks.
+A step is one einsum call (one fused launch on the contraction routes) through
+the public EinsumBuilder runner over one BASELINE config, inputs resident in
+HBM. Under torchrun the config's leading output axis is split over the ranks
+with the product's shard plan (pto_einsum.distributed): strong scaling, the
+job does the config's work once, with no collective on the data path; the
+weak-scaling figure (every rank the whole config) and the optional NCCL
+all-gather of the result are reported beside it. Timing: CUDA events on the
+launching stream around exactly K steps, bracketed by a barrier and
+torch.cuda.synchronize(), max over ranks.
 
-Default config is BASELINE config 2 ('bij,bjk->bik' fp16 -> fp32, b=64,
-i=j=k=1024), the contraction the metric is quoted on; --config selects the
-others (names in tests/corpus.py CONFIGS). Inputs are synthetic, seeded.
+The headline is BASELINE config 2 ('bij,bjk->bik' fp16 -> fp32, b=64,
+i=j=k=1024), the contraction the metric is quoted on; every other config
+(names in tests/corpus.py CONFIGS) is measured into the line's `configs` map
+with its own roofline, end-to-end figure, CPU baseline and sampled parity
+against the CPU oracle. Inputs are synthetic, seeded, generated on the device.
 
 --impl reference times the reference's own CPU implementation (the libraries
 oracle/build_ref.py compiled from the reference sources, oracle/_ref) on all
@@ -34,14 +40,18 @@ sys.path.insert(0, os.path.join(REPO, "tests"))
 
 import torch  # noqa: E402
 
-from corpus import CONFIGS  # noqa: E402
+import fullsize  # noqa: E402
 
-CFG = {name: (eq, s0, s1, dt) for name, eq, s0, s1, dt in CONFIGS}
+CFG = fullsize.CFG   # name -> (equation, shape0, shape1, dtype name); --shrink edits it in place
+L2_BYTES = 126 << 20
 
 # per config: (metric kind, bound, unit of work per call)
 #   flops = 2*I*L0*L1*C; bytes = inputs read once + fp32 output written once
-def work(name):
-    eq, s0, s1, dt = CFG[name]
+def work(name, s0=None, s1=None):
+    """Units of config `name` (or of its shard with shapes s0, s1) per call:
+    flops = 2*I*L0*L1*C; bytes = inputs read once + fp32 output written once."""
+    eq, f0, f1, dt = CFG[name]
+    s0, s1 = tuple(s0 or f0), tuple(s1 or f1)
     from pto_einsum import planner
     r, _ = planner.choose_operand_order("cuda", eq, s0, s1)
     es = 2 if dt == "float16" else 4
@@ -52,7 +62,7 @@ def work(name):
         n1 *= d
     nbytes = es * (n0 + n1) + 4 * r["n_elem"]
     if r["elementwise"] or r["broadcast"]:
-        return dict(kind="bytes", bound="hbm", flops=0, bytes=nbytes, recipe=r)
+        return dict(kind="bytes", bound="hbm", flops=0, bytes=nbytes, recipe=r, units=nbytes)
     flops = 2 * r["I"] * r["L0"] * r["L1"] * r["C"]
     # Contractions report TFLOP/s (BASELINE metric). The binding roof is the
     # larger of the two floors: tensor time at the measured peak (fp32 via
@@ -63,45 +73,14 @@ def work(name):
     t_tensor = flops / (tensor_peak * 1e12)
     t_hbm = nbytes / (hbm * 1e9)
     bound = "tensor" if t_tensor >= 0.9 * t_hbm else "hbm"
-    return dict(kind="flops", bound=bound, flops=flops, bytes=nbytes, recipe=r, tensor_peak=tensor_peak)
+    return dict(kind="flops", bound=bound, flops=flops, bytes=nbytes, recipe=r, tensor_peak=tensor_peak,
+                units=flops)
 
 
 def metric_of(w):
     if w["kind"] == "flops":
         return "einsum TFLOP/s", "TFLOP/s"
     return "einsum HBM GB/s", "GB/s"
-
-
-def make_inputs(name, device, rank):
-    eq, s0, s1, dt = CFG[name]
-    dtype = getattr(torch, dt)
-    g = torch.Generator(device="cpu").manual_seed(1000 + rank)
-    if name in ("cfg2",):
-        a = torch.rand(s0, generator=g, dtype=torch.float32)
-        b = torch.rand(s1, generator=g, dtype=torch.float32)
-    elif name == "cfg4b":
-        a = torch.randn(s0, generator=g, dtype=torch.float32)
-        t = torch.arange(s0[0], dtype=torch.float32)
-        diff = t[:, None] - t[None, :]
-        b = torch.where(diff >= 0, torch.pow(torch.tensor(0.99), diff.clamp(min=0)), torch.zeros(()))
-    elif name == "cfg5_rms":
-        a = torch.randn(s0, generator=g)
-        b = torch.rand(s1, generator=g) + 0.5
-    elif name == "cfg5_rope":
-        a = torch.randn(s0, generator=g)
-        S, D = s1
-        pos = torch.arange(S, dtype=torch.float64)[:, None]
-        j = torch.arange(D // 2, dtype=torch.float64)[None, :]
-        ang = pos * torch.pow(10000.0, -2.0 * j / D)
-        b = torch.cat([torch.cos(ang), torch.sin(ang)], dim=1).float()
-    elif name == "cfg5_alibi":
-        a = torch.randn(s0, generator=g)
-        H = s1[0]
-        b = torch.pow(2.0, -8.0 * (torch.arange(H, dtype=torch.float64) + 1) / H).float()
-    else:
-        a = torch.randn(s0, generator=g)
-        b = torch.randn(s1, generator=g)
-    return a.to(dtype).to(device), b.to(dtype).to(device)
 
 
 class Clocks:
@@ -129,16 +108,13 @@ class Clocks:
         for line in self.proc.stdout:
             self.lines.append((time.time(), line.strip()))
 
-    def stop(self, t0, t1):
+    def summary(self, t0, t1):
+        """Median SM clock, max clock and active throttle reasons of the samples
+        taken in wall-clock window [t0, t1]."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
         rows = []
-        for ts, line in self.lines:
+        for ts, line in list(self.lines):
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -150,6 +126,15 @@ class Clocks:
         reasons = sorted({names[k] for _, f in inside for k in range(4) if f[5 + k] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(inside)}
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
 
 
 def peaks():
@@ -226,7 +211,7 @@ def run_reference_arm(args, rank, world):
     value = statistics.median(vals)
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(times), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": name, "equation": CFG[name][0], "shape0": CFG[name][1],
                        "shape1": CFG[name][2], "input_dtype": CFG[name][3]},
@@ -540,19 +525,242 @@ def run_gdn_suite(args):
         print(json.dumps(row))
 
 
+
+
+def _max_over_ranks(x, dist, device):
+    if not dist:
+        return x
+    t = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(dist, device):
+    torch.cuda.synchronize(device)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+
+
+def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True, cpu=False, parity=True,
+            e2e=True):
+    """Time config `name` through the public EinsumBuilder runner.
+
+    shard=True: the config's leading output axis is split over the ranks with
+    the product's shard plan (pto_einsum.distributed.shard_operands), so the
+    job does the config's work once (strong scaling). shard=False: every rank
+    runs the whole config (weak scaling). Inputs are generated on the device
+    from seeded generators (the shards concatenate to the one-device inputs)."""
+    from pto_einsum import EinsumBuilder, _core
+    from pto_einsum.distributed import shard_operands
+    eq, _, _, dt = CFG[name]
+    dtype = getattr(torch, dt)
+    full = work(name)
+    metric, unit = metric_of(full)
+    a, b = fullsize.make_inputs(name, device=device)
+    if shard and world > 1:
+        a, b = shard_operands(eq, a, b, rank, world)
+    ls0, ls1 = tuple(a.shape), tuple(b.shape)
+    local = work(name, ls0, ls1)
+    job_units = full["units"] if shard else full["units"] * world
+    builder = EinsumBuilder(eq, [ls0, ls1], dtype, device=device)
+    run = builder.build()
+    stream = torch.cuda.current_stream(device)
+    out_bytes = 4 * local["recipe"]["n_elem"]
+    in_bytes = a.numel() * a.element_size() + b.numel() * b.element_size()
+    # Consecutive steps must not find their data in L2: below twice the L2 size
+    # the step rotates over several input sets (and keeps that many outputs
+    # alive, so the allocator hands out distinct output blocks).
+    foot = in_bytes + out_bytes
+    nsets = 1 if foot >= 2 * L2_BYTES else min(16, -(-2 * L2_BYTES // foot))
+    sets = [(a, b)] + [(a.clone(), b.clone()) for _ in range(nsets - 1)]
+    l2_note = ("inputs+output larger than 2x L2 (126 MB)" if nsets == 1 else
+               f"rotating {nsets} input/output sets of {foot / 1e6:.0f} MB ({nsets * foot / 1e6:.0f} MB > 2x L2)")
+    outs = [None] * nsets
+    for k in range(max(args.warmup, 3)):
+        outs[k % nsets] = run(*sets[k % nsets])
+    torch.cuda.synchronize(device)
+    # clock window: untimed back-to-back steps before and after the timed region
+    # so the nvidia-smi samples (every 50 ms) see the GPU under this load
+    per_step_s = 1e-3 * max(_time(lambda: run(*sets[0]), 3, 1), 1e-3)
+    roll = max(1, int(0.25 / per_step_s))
+    _barrier(dist, device)
+    t_win0 = time.time()
+    for k in range(roll):
+        outs[k % nsets] = run(*sets[k % nsets])
+    _barrier(dist, device)
+    launches0 = _core.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(steps):
+        j = k % nsets
+        evs[k][0].record(stream)
+        outs[j] = run(*sets[j])
+        evs[k][1].record(stream)
+    stop.record(stream)
+    torch.cuda.synchronize(device)
+    launches = _core.launch_count() - launches0
+    for k in range(roll):
+        outs[k % nsets] = run(*sets[k % nsets])
+    torch.cuda.synchronize(device)
+    t_win1 = time.time()
+    _barrier(dist, device)
+    elapsed_ms = _max_over_ranks(start.elapsed_time(stop), dist, device)
+    per_launch_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    clk = clocks.summary(t_win0, t_win1)
+    assert _core.device_error(stream.cuda_stream) == 0, "device error word set"
+    scale = 1e12 if full["kind"] == "flops" else 1e9
+    value = job_units * steps / (elapsed_ms * 1e-3) / scale
+
+    hbm, tflops, peak_src = peaks()
+    if full["bound"] == "tensor":
+        achieved = local["flops"] / (per_launch_ms * 1e-3) / 1e12
+        peak = full.get("tensor_peak", tflops)
+        if peak != tflops:
+            peak_src += " (fp32 3xTF32: bf16 peak / 6)"
+    else:
+        achieved = local["bytes"] / (per_launch_ms * 1e-3) / 1e9
+        peak = hbm
+    traffic = traffic_of(name)
+    traffic_note = "ncu dram read+write bytes of one full-size launch"
+    if traffic is not None and local["units"] != full["units"]:
+        traffic = traffic * local["units"] / full["units"]
+        traffic_note = "full-size launch's ncu dram bytes scaled by this rank's share of the work"
+    res = {"metric": metric, "unit": unit, "value": value, "ms_per_step": elapsed_ms / steps, "steps": steps,
+           "dtype": "f16" if dt == "float16" else "f32",
+           "config": {"workload": name, "equation": eq, "shape0": list(CFG[name][1]),
+                      "shape1": list(CFG[name][2]), "local_shape0": list(ls0), "local_shape1": list(ls1),
+                      "input_dtype": dt, "output_dtype": "float32", "l2": l2_note},
+           "roofline": {"bound": full["bound"], "achieved": achieved, "peak": peak,
+                        "unit": "TFLOP/s" if full["bound"] == "tensor" else "GB/s",
+                        "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                        "traffic_source": traffic_note, "per_launch_ms": per_launch_ms},
+           "gpu_launches": launches, "clocks": clk}
+
+    if parity and rank == 0:
+        out = run(a, b)
+        chk = fullsize.check(name, a.cpu(), b.cpu(), out.cpu(), threads=min(os.cpu_count() or 1, 32),
+                             whole_exact=False)
+        chk["tolerance"] = 0.0 if name in fullsize.EXACT else fullsize.TOL[dt]
+        chk["pass"] = chk["bit_exact"] if name in fullsize.EXACT else chk["rel_frobenius"] <= chk["tolerance"]
+        chk["oracle"] = "oracle/einsum_oracle.c (restates the reference include/cpu_einsum.h:53-92)"
+        res["parity"] = chk
+        del out
+    del outs, sets
+    torch.cuda.empty_cache()
+
+    if e2e:
+        res["e2e"] = e2e_run(run, a, b, local, job_units, scale, unit, args, dist, device)
+    if cpu and rank == 0 and world == 1:
+        r = cpu_reference(name)
+        if r:
+            res["cpu_baseline"] = {"value": r[0], "unit": unit, "cores": r[1], "kind": "reference",
+                                   "sample": r[2]}
+    builder.cleanup()
+    del a, b
+    torch.cuda.empty_cache()
+    return res
+
+
+def e2e_run(run, a, b, local, job_units, scale, unit, args, dist, device):
+    """The same runner call end to end with host buffers: each step copies its
+    inputs from pinned host memory and its result back inside the timed region.
+    Pipelined the way a streaming caller runs it: host->device copies of step
+    k+1 and device->host copies of step k-1 on their own streams while step k
+    computes (PCIe is full duplex); device inputs double-buffered."""
+    stream = torch.cuda.current_stream(device)
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    out_h = torch.empty(local["recipe"]["out_shape"], dtype=torch.float32).pin_memory()
+    step_bytes = a_h.numel() * a_h.element_size() + b_h.numel() * b_h.element_size() + out_h.numel() * 4
+    e_steps = max(2, min(args.e2e_steps, int(8e9 // max(step_bytes, 1))))
+    s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ad = [torch.empty_like(a), torch.empty_like(a)]
+    bd = [torch.empty_like(b), torch.empty_like(b)]
+    h2d_done = [torch.cuda.Event(), torch.cuda.Event()]
+    comp_done = [torch.cuda.Event(), torch.cuda.Event()]
+
+    def step(k):
+        j = k % 2
+        if k >= 2:
+            s_h2d.wait_event(comp_done[j])   # buffer j free once step k-2 computed
+        with torch.cuda.stream(s_h2d):
+            ad[j].copy_(a_h, non_blocking=True)
+            bd[j].copy_(b_h, non_blocking=True)
+            h2d_done[j].record(s_h2d)
+        stream.wait_event(h2d_done[j])
+        with torch.cuda.stream(stream):
+            o = run(ad[j], bd[j])
+            comp_done[j].record(stream)
+        s_d2h.wait_event(comp_done[j])
+        with torch.cuda.stream(s_d2h):
+            out_h.copy_(o, non_blocking=True)
+            o.record_stream(s_d2h)
+
+    step(0)  # warm-up
+    _barrier(dist, device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e0.record(s_h2d)
+    for k in range(e_steps):
+        step(k)
+    e1 = torch.cuda.Event(enable_timing=True)
+    s_d2h.wait_stream(stream)
+    e1.record(s_d2h)
+    torch.cuda.synchronize(device)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
+    del ad, bd
+    return {"value": job_units * e_steps / (e2e_ms * 1e-3) / scale, "unit": unit,
+            "h2d_bytes_per_step": a_h.numel() * a_h.element_size() + b_h.numel() * b_h.element_size(),
+            "d2h_bytes_per_step": out_h.numel() * 4, "steps": e_steps,
+            "note": "per rank; value = the job's work per step x steps / max-over-ranks time"}
+
+
+def measure_gather(name, args, rank, world, dist, device):
+    """Optional result-on-every-rank path: sharded_einsum(gather=True) (this
+    rank's shard, then one NCCL all-gather over NVLink), timed on its own
+    against the shard compute alone. Max over ranks."""
+    from pto_einsum.distributed import shard_operands, shard_plan, sharded_einsum
+    eq = CFG[name][0]
+    a, b = fullsize.make_inputs(name, device=device)
+    full_size = shard_plan(eq, a.shape, b.shape)[3]
+    a, b = shard_operands(eq, a, b, rank, world)
+    from pto_einsum import EinsumBuilder
+    run = EinsumBuilder(eq, [a.shape, b.shape], a.dtype, device=device).build()
+    compute = lambda e, x, y: run(x, y)  # noqa: E731
+    reps = 10
+    for _ in range(3):
+        sharded_einsum(eq, a, b, full_size=full_size, gather=True, compute=compute)
+    _barrier(dist, device)
+    t_compute = _max_over_ranks(_time(lambda: run(a, b), reps, 2), dist, device)
+    _barrier(dist, device)
+    t_gather = _max_over_ranks(_time(lambda: sharded_einsum(eq, a, b, full_size=full_size, gather=True,
+                                                            compute=compute), reps, 2), dist, device)
+    full_out = sharded_einsum(eq, a, b, full_size=full_size, gather=True, compute=compute)
+    nbytes = full_out.numel() * 4
+    return {"ms_compute_shard": t_compute, "ms_compute_and_allgather": t_gather,
+            "ms_allgather": t_gather - t_compute, "output_bytes": nbytes,
+            "allgather_busbw_GBps": nbytes * (world - 1) / world / ((t_gather - t_compute) * 1e-3) / 1e9
+            if t_gather > t_compute else None,
+            "how": "sharded_einsum(gather=True): shard einsum + NCCL all_gather of padded shards + trim; "
+                   "CUDA events, 10 calls, max over ranks"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=sorted(CFG))
+    ap.add_argument("--configs", default="all",
+                    help="also measure these configs into the line's `configs` map: all, none, or a comma list")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16,
                     help="pipelined end-to-end steps (fill and drain cost about one step)")
     ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin"],
-                    help="instead of the one-line benchmark: time the LLM contraction patterns and the "
-                         "linear-attention chain against torch.einsum (one JSON line per op)")
+                    help="instead of the one-line benchmark: one JSON line per op of that suite")
     ap.add_argument("--shrink", type=int, default=1,
                     help="divide the config's leading axis (small cases for profiler captures)")
     args = ap.parse_args()
@@ -571,172 +779,60 @@ def main():
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return
-    if args.suite == "callers":
-        run_callers_suite(args)
-        return
-    if args.suite == "permute":
-        run_permute_suite(args)
-        return
-    if args.suite == "gdn":
-        run_gdn_suite(args)
-        return
-    if args.suite == "base":
-        run_base_suite(args)
-        return
-    if args.suite == "thin":
-        run_thin_suite(args)
+    suites = {"callers": run_callers_suite, "permute": run_permute_suite, "gdn": run_gdn_suite,
+              "base": run_base_suite, "thin": run_thin_suite}
+    if args.suite:
+        suites[args.suite](args)
         return
 
     dist = None
-    if world > 1:
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-
-    from pto_einsum import EinsumBuilder, _core
-    name = args.config
-    eq, s0, s1, dt = CFG[name]
-    dtype = getattr(torch, dt)
-    w = work(name)
-    metric, unit = metric_of(w)
-    a, b = make_inputs(name, device, rank)
-    builder = EinsumBuilder(eq, [s0, s1], dtype, device=device)
-    run = builder.build()
-    stream = torch.cuda.current_stream(device)
-
-    for _ in range(args.warmup):
-        out = run(a, b)
-    torch.cuda.synchronize(device)
-    del out
-
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
     clocks = Clocks(local)
     clocks.start()
     time.sleep(0.2)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    launches0 = _core.launch_count()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    t_wall0 = time.time()
-    start = torch.cuda.Event(enable_timing=True)
-    stop = torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for k in range(args.steps):
-        evs[k][0].record(stream)
-        out = run(a, b)
-        evs[k][1].record(stream)
-    stop.record(stream)
-    torch.cuda.synchronize(device)
-    t_wall1 = time.time()
-    if dist:
-        dist.barrier()
-    launches = _core.launch_count() - launches0
-    elapsed_ms = start.elapsed_time(stop)
-    per_launch_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
-    clk = clocks.stop(t_wall0, t_wall1)
-    if dist:
-        t = torch.tensor([elapsed_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    assert _core.device_error(stream.cuda_stream) == 0, "device error word set"
 
-    units_per_step = w["flops"] if w["kind"] == "flops" else w["bytes"]
-    scale = 1e12 if w["kind"] == "flops" else 1e9
-    value = units_per_step * args.steps * world / (elapsed_ms * 1e-3) / scale
+    name = args.config
+    want_cpu = not args.no_cpu_baseline
+    head = measure(name, args, rank, world, dist, device, clocks, steps=args.steps, cpu=want_cpu,
+                   parity=not args.no_parity)
+    extra = {}
+    if world > 1:
+        weak = measure(name, args, rank, world, dist, device, clocks, steps=args.steps, shard=False,
+                       parity=False, e2e=False)
+        extra["weak_scaling"] = {"value": weak["value"], "unit": weak["unit"], "ms_per_step": weak["ms_per_step"],
+                                 "global_batch": CFG[name][1][0] * world,
+                                 "how": "every rank runs the whole config (no sharding), max-over-ranks time"}
+        extra["allgather"] = measure_gather(name, args, rank, world, dist, device)
+    others = []
+    if args.configs != "none":
+        others = [n for n in CFG if n != name and n != "cfg1"] if args.configs == "all" else \
+            [n for n in args.configs.split(",") if n and n != name]
+    cmap = {}
+    for n in others:
+        cmap[n] = measure(n, args, rank, world, dist, device, clocks, steps=args.steps, cpu=want_cpu,
+                          parity=not args.no_parity)
+    clocks.stop()
 
-    # ---- end to end through the public API with host buffers ----
-    a_h = a.cpu().pin_memory()
-    b_h = b.cpu().pin_memory()
-    out_h = torch.empty(w["recipe"]["out_shape"], dtype=torch.float32).pin_memory()
-    del out
-    torch.cuda.synchronize(device)
-    # Pipelined the way a streaming caller would: H2D of step k+1 and D2H of
-    # step k-1 run on their own streams while step k computes (PCIe is full
-    # duplex); device inputs are double-buffered. Every step still copies its
-    # inputs in and its result out inside the timed region.
-    e_steps = max(2, args.e2e_steps)
-    s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    ad = [torch.empty_like(a), torch.empty_like(a)]
-    bd = [torch.empty_like(b), torch.empty_like(b)]
-    h2d_done = [torch.cuda.Event(), torch.cuda.Event()]
-    comp_done = [torch.cuda.Event(), torch.cuda.Event()]
-
-    def e2e_step(k):
-        j = k % 2
-        if k >= 2:
-            s_h2d.wait_event(comp_done[j])   # buffer j free once step k-2 computed
-        with torch.cuda.stream(s_h2d):
-            ad[j].copy_(a_h, non_blocking=True)
-            bd[j].copy_(b_h, non_blocking=True)
-            h2d_done[j].record(s_h2d)
-        stream.wait_event(h2d_done[j])
-        with torch.cuda.stream(stream):
-            o = run(ad[j], bd[j])
-            comp_done[j].record(stream)
-        s_d2h.wait_event(comp_done[j])
-        with torch.cuda.stream(s_d2h):
-            out_h.copy_(o, non_blocking=True)
-            o.record_stream(s_d2h)
-
-    e2e_step(0)  # warm-up
-    torch.cuda.synchronize(device)
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e0.record(s_h2d)
-    for k in range(e_steps):
-        e2e_step(k)
-    e1 = torch.cuda.Event(enable_timing=True)
-    s_d2h.wait_stream(stream)
-    e1.record(s_d2h)
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_value = units_per_step * e_steps * world / (e2e_ms * 1e-3) / scale
-
-    hbm, tflops, peak_src = peaks()
-    if w["bound"] == "tensor":
-        achieved = w["flops"] / (per_launch_ms * 1e-3) / 1e12
-        peak = w.get("tensor_peak", tflops)
-        if peak != tflops:
-            peak_src += " (fp32 3xTF32: bf16 peak / 6)"
-    else:
-        achieved = w["bytes"] / (per_launch_ms * 1e-3) / 1e9
-        peak = hbm
-    traffic = traffic_of(name)
-
-    line = None
     if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu_baseline:
-            r = cpu_reference(name)
-            if r:
-                cpu = {"value": r[0], "unit": unit, "cores": r[1], "kind": "reference", "sample": r[2]}
+        lead = CFG[name][1][0]
         line = {
-            "metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16" if dt == "float16" else "f32",
-            "data": "synthetic (seeded)",
-            "config": {"workload": name, "equation": eq, "shape0": s0, "shape1": s1, "input_dtype": dt,
-                       "output_dtype": "float32", "global_batch": s0[0] * world,
-                       "parallelism": f"batch-sharded x{world}, no collective",
-                       "l2": "inputs+output larger than L2 (126 MB)"},
-            "roofline": {"bound": w["bound"], "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s" if w["bound"] == "tensor" else "GB/s",
-                         "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": unit,
-                    "h2d_bytes_per_step": a.numel() * a.element_size() + b.numel() * b.element_size(),
-                    "d2h_bytes_per_step": out_h.numel() * 4},
-            "gpu_launches": launches,
-            "clocks": clk,
+            "metric": head["metric"], "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": head["dtype"],
+            "data": "synthetic (seeded, generated on the device)",
+            "config": dict(head["config"], global_batch=lead,
+                           parallelism=f"leading axis sharded over {world} GPU(s) "
+                                       "(pto_einsum.distributed.shard_operands), no collective on the data path"),
+            "roofline": head["roofline"], "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"],
+            "parity": head.get("parity"), "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
         }
+        line.update(extra)
+        if cmap:
+            line["configs"] = {n: {k: v for k, v in r.items() if k not in ("metric",)} for n, r in cmap.items()}
         print(json.dumps(line))
     if dist:
         dist.barrier()

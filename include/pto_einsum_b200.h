@@ -123,7 +123,10 @@ int pe_batched_matmul(int32_t dtype, int64_t I, int64_t L0, int64_t L1, int64_t 
  *    with PE_ERR_WORKSPACE before anything is launched.
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress) with that device current; make that first call
- *    before any stream capture.
+ *    before any stream capture. The address is cached per device for the life
+ *    of the process; it is not valid after cudaDeviceReset (or after the
+ *    primary context is released and created again), so do not call this
+ *    entry point after resetting a device.
  *  - All calls share the one array: calls whose kernels can overlap on the GPU
  *    (different streams, or several host threads) race on it and must be
  *    serialised by the caller. Nothing in it needs to start zeroed; every

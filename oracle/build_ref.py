@@ -28,8 +28,12 @@ from ref_specs import SPECS  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("PTO_EINSUM_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("PTO_EINSUM_REFERENCE"),
+                    help="reference checkout (default: $PTO_EINSUM_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        print("no reference checkout given (--reference or PTO_EINSUM_REFERENCE); oracle/_ref not built")
+        return 0
     src = os.path.join(args.reference, "src")
     if not os.path.isdir(src):
         print(f"reference sources not found at {src}; oracle/_ref not built")

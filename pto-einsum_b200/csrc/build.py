@@ -42,25 +42,36 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile each source to an object in parallel, then link the library."""
     if not force and not needs_build():
         return OUT
+    import tempfile
+    from concurrent.futures import ThreadPoolExecutor
     os.makedirs(OUT_DIR, exist_ok=True)
     nvcc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "bin", "nvcc")
     tag = source_hash()
-    objs = []
     tmp = OUT + ".tmp"
-    cmd = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-           "-I", INCLUDE, "-I", HERE, f'-DPE_BUILD_TAG="{tag}"',
-           *[os.path.join(HERE, s) for s in SOURCES], "-o", tmp]
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+             "-I", INCLUDE, "-I", HERE, f'-DPE_BUILD_TAG="{tag}"']
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
-    if verbose:
-        sys.stderr.write(r.stderr)
+        flags.append("-Xptxas=-v")
+    with tempfile.TemporaryDirectory(prefix="pe_build_") as td:
+        objs = [os.path.join(td, s.replace(".cu", ".o")) for s in SOURCES]
+
+        def one(k):
+            return subprocess.run([nvcc, *flags, "-c", os.path.join(HERE, SOURCES[k]), "-o", objs[k]],
+                                  capture_output=True, text=True)
+        with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+            results = list(ex.map(one, range(len(SOURCES))))
+        for r in results:
+            if r.returncode != 0:
+                raise RuntimeError("nvcc failed:\n" + r.stdout + r.stderr)
+            if verbose:
+                sys.stderr.write(r.stderr)
+        r = subprocess.run([nvcc, *ARCH, "-shared", *objs, "-o", tmp], capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("nvcc link failed:\n" + r.stdout + r.stderr)
     os.replace(tmp, OUT)
-    del objs
     return OUT
 
 

@@ -12,11 +12,14 @@ Public surface and behaviour follow the reference ``src/pto_einsum/builder.py``:
 
 Differences, all deliberate:
 
-* the backend is CUDA (sm_100a). ``device`` is ``"cuda"``, ``"cuda:N"`` or a
-  ``torch.device``; ``"npu"`` is accepted as an alias of the current CUDA
-  device so reference call sites run unchanged. ``device="cpu"`` plans (the
-  planner is device-aware exactly like the reference) but does not execute:
-  the CPU reference path is the parity oracle, kept outside this package.
+* the accelerator backend is CUDA (sm_100a). ``device`` is ``"cuda"``,
+  ``"cuda:N"`` or a ``torch.device``; ``"npu"`` is accepted as an alias of the
+  current CUDA device so reference call sites run unchanged.
+* ``device="cpu"`` plans with the reference's CPU semantics (no broadcast
+  route) and runs a host library generated from ``include/pto_einsum_cpu.h``
+  (g++, no FMA contraction, host threads), bit-identical to the reference CPU
+  path (:606-626, :704-709, :856-875); float16 is rejected there as in the
+  reference.
 * the generated library is a g++-compiled C++ shim that forwards to the
   prebuilt core library, so a cache miss costs ~0.3 s instead of an nvcc run.
 * the batched partial-tile guard (:588-604) is not raised: the CUDA kernels
@@ -213,23 +216,22 @@ class EinsumBuilder:
         )
 
     # ---- code generation ------------------------------------------------------
-    def _require_cuda_backend(self):
-        if self._plan_device == "cpu":
-            raise ValueError(
-                "pto_einsum (B200) executes on CUDA only; device='cpu' selects the reference CPU "
-                "path, which this project keeps as its parity oracle (oracle/), not as a backend")
-
     def generate_code(self):
-        self._require_cuda_backend()
+        on_cpu = self._plan_device == "cpu"
         if self.dtype == torch.float32:
             data_t, self.c_type, pe_dtype = 'float', ctypes.c_float, PE_F32
         elif self.dtype == torch.float16:
+            if on_cpu:
+                raise TypeError("float16 is not supported on CPU")
             data_t, self.c_type, pe_dtype = 'half', ctypes.c_uint16, PE_F16
         else:
             raise TypeError(f"Unsupported torch dtype: {self.dtype}")
         if self.recipe is None:
             self.parse_equation()
         r = self.recipe
+        if on_cpu:
+            self._generate_cpu_code(data_t)
+            return
         prelude = templates.PRELUDE.format(
             equation=self.equation.replace('\n', ' '), shapes=[tuple(s) for s in self.input_shapes],
             dtype=str(self.dtype), core=core_version(), pe_dtype=pe_dtype)
@@ -262,8 +264,32 @@ class EinsumBuilder:
         self.code_hash = hashlib.md5(code.encode('utf-8')).hexdigest()
         self.target_dir = os.path.join(self.build_base, self.code_hash)
 
+    def _generate_cpu_code(self, data_t):
+        """device="cpu": a host library computing with pto_einsum_cpu.h, bit-identical
+        to the reference CPU path (on CPU the planner never takes the broadcast route,
+        builder.py:373-376 of the reference)."""
+        r = self.recipe
+        prelude = templates.CPU_PRELUDE.format(
+            equation=self.equation.replace('\n', ' '), shapes=[tuple(s) for s in self.input_shapes],
+            dtype=str(self.dtype))
+        if r['elementwise']:
+            cfg = templates.ELEMENTWISE_CONFIG.format(N=r['n_elem'])
+            code = templates.CPU_ELEMENTWISE_LIB.format(prelude=prelude, config_code=cfg, data_t=data_t)
+        else:
+            shape0, shape1 = self._exec_shapes
+            names = ('config_tpose_inp0', 'config_tpose_inp1', 'config_tpose_out')
+            t0 = templates.PERMUTE_CONFIG.format(**self.transpose_config_gen(names[0], shape0, r['in_transpose_idxs'][0]))
+            t1 = templates.PERMUTE_CONFIG.format(**self.transpose_config_gen(names[1], shape1, r['in_transpose_idxs'][1]))
+            to = templates.PERMUTE_CONFIG.format(**self.transpose_config_gen(
+                names[2], r['out_interpret_shape'], r['out_transpose_idxs']))
+            ec = templates.EINSUM_CONFIG.format(**self.einsum_config_gen(*names))
+            code = templates.CPU_MATMUL_LIB.format(prelude=prelude, tpose_inp0_code=t0, tpose_inp1_code=t1,
+                                                   tpose_out_code=to, einsum_code=ec, data_t=data_t)
+        self.cpp_code = code
+        self.code_hash = hashlib.md5(code.encode('utf-8')).hexdigest()
+        self.target_dir = os.path.join(self.build_base, self.code_hash)
+
     def compile(self):
-        self._require_cuda_backend()
         os.makedirs(self.target_dir, exist_ok=True)
         extra = os.environ.get("EINSUM_EXTRA_DEFINES", "").split()
         tag = "_" + hashlib.md5(" ".join(extra).encode()).hexdigest()[:8] if extra else ""
@@ -275,21 +301,34 @@ class EinsumBuilder:
             f.write(self.cpp_code)
         cxx = os.environ.get("CXX", "g++")
         tmp = f"{self.so_filename}.{os.getpid()}.tmp"
-        cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", "-I", self.include_dir, *extra,
-               self.cpp_filename, "-o", tmp, "-L", LIB_DIR, "-lpto_einsum_b200",
-               f"-Wl,-rpath,{LIB_DIR}"]
+        if self._plan_device == "cpu":
+            # no FMA contraction: every product and sum rounds once, as on the reference
+            cmd = [cxx, "-O3", "-ffp-contract=off", "-fno-fast-math", "-shared", "-fPIC", "-std=c++17",
+                   "-pthread", "-I", self.include_dir, *extra, self.cpp_filename, "-o", tmp]
+        else:
+            cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", "-I", self.include_dir, *extra,
+                   self.cpp_filename, "-o", tmp, "-L", LIB_DIR, "-lpto_einsum_b200",
+                   f"-Wl,-rpath,{LIB_DIR}"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"Compilation failed:\n{res.stderr}")
         os.replace(tmp, self.so_filename)  # atomic: concurrent builders never see a partial .so
 
     def load_library(self):
-        core_lib()  # the shim resolves its pe_* symbols against the core library
-        self.lib = ctypes.CDLL(self.so_filename)
         P = ctypes.POINTER
         T = self.c_type
         fp = P(ctypes.c_float)
         r = self.recipe
+        if self._plan_device == "cpu":
+            # host library: run_einsum only (synchronous), like the reference's CPU .so
+            self.lib = ctypes.CDLL(self.so_filename)
+            self.lib.run_einsum.argtypes = [ctypes.c_void_p] * 4
+            self.lib.run_einsum.restype = None
+            self.lib.run_einsum_last_error.argtypes = []
+            self.lib.run_einsum_last_error.restype = ctypes.c_int
+            return
+        core_lib()  # the shim resolves its pe_* symbols against the core library
+        self.lib = ctypes.CDLL(self.so_filename)
         if not r['elementwise'] and not r['broadcast']:
             for name in ('run_transpose_inp0', 'run_transpose_inp1'):
                 fn = getattr(self.lib, name)
@@ -346,6 +385,8 @@ class EinsumBuilder:
         shapes = (tuple(self.input_shapes[0]), tuple(self.input_shapes[1]))
         dtype = self.dtype
         swap = self._swap_operands
+        if self._plan_device == "cpu":
+            return self._cpu_runner(shapes, out_shape)
         exec_fn = self.lib.run_einsum_exec
         last_error = self.lib.run_einsum_last_error
 
@@ -390,6 +431,39 @@ class EinsumBuilder:
                     exec_fn(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
             if last_error():
                 self._check("run_einsum_exec")
+            return out
+
+        return run
+
+    def _cpu_runner(self, shapes, out_shape):
+        """Runner of a device="cpu" build: host tensors in, a host fp32 tensor out,
+        computed synchronously (reference builder.py:856-875)."""
+        dtype, swap = self.dtype, self._swap_operands
+
+        def run(*operands):
+            if len(operands) != 2:
+                raise ValueError("Expected exactly two operands.")
+            inp0, inp1 = operands
+            if inp0.shape != shapes[0] or inp1.shape != shapes[1]:
+                raise ValueError(
+                    f"Input shapes {inp0.shape} and {inp1.shape} do not match built shapes {self.input_shapes}.")
+            if inp0.dtype != dtype or inp1.dtype != dtype:
+                raise TypeError(
+                    f"Input datatypes {inp0.dtype} and {inp1.dtype} do not match built datatype {dtype}.")
+            if inp0.device.type != 'cpu' or inp1.device.type != 'cpu':
+                raise ValueError(f"pto_einsum: a device='cpu' build takes host tensors (got {inp0.device}, "
+                                 f"{inp1.device})")
+            if self.lib is None:
+                raise RuntimeError("pto_einsum: runner called after cleanup()")
+            inp0, inp1 = inp0.contiguous(), inp1.contiguous()
+            if swap:
+                inp0, inp1 = inp1, inp0
+            out = torch.zeros(out_shape, dtype=torch.float32, device="cpu")
+            if out.numel() == 0:
+                return out
+            self.lib.run_einsum(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), None)
+            if self.lib.run_einsum_last_error():
+                raise MemoryError(f"pto_einsum: host buffers for '{self.equation}' could not be allocated")
             return out
 
         return run

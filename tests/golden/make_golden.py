@@ -36,12 +36,14 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 from corpus import ALL_SMALL, BATCHED_PARTIAL, CONFIGS, case_id  # noqa: E402
 
-REF = os.environ.get("PTO_EINSUM_REFERENCE", "/root/reference")
+REF = os.environ.get("PTO_EINSUM_REFERENCE")  # the reference checkout (required)
 FULL_LIMIT = 8192        # outputs up to this many elements are stored whole
 N_SAMPLES = 512
 
 
 def load_reference():
+    if not REF or not os.path.isdir(os.path.join(REF, "src")):
+        raise SystemExit("set PTO_EINSUM_REFERENCE to the reference checkout (the directory holding src/)")
     sys.modules.setdefault("torch_npu", types.ModuleType("torch_npu"))
     sys.path.insert(0, os.path.join(REF, "src"))
     from pto_einsum import builder as ref_builder  # noqa: E402

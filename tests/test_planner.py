@@ -94,12 +94,12 @@ def test_validation_messages():
         planner.parse_recipe("cuda", "ij,jk->k", (32, 64), (64, 128))
 
 
-def test_unsupported_dtype_and_cpu_device():
+def test_unsupported_dtype_and_cpu_float16():
     b = EinsumBuilder("ij,jk->ik", [(32, 64), (64, 32)], torch.bfloat16)
     b.parse_equation()
     with pytest.raises(TypeError, match="Unsupported torch dtype"):
         b.generate_code()
-    c = EinsumBuilder("ij,jk->ik", [(32, 64), (64, 32)], torch.float32, device="cpu")
+    c = EinsumBuilder("ij,jk->ik", [(32, 64), (64, 32)], torch.float16, device="cpu")
     c.parse_equation()  # planning works for every device
-    with pytest.raises(ValueError, match="CUDA only"):
+    with pytest.raises(TypeError, match="float16 is not supported on CPU"):
         c.generate_code()

@@ -65,18 +65,46 @@ def lib():
     return L
 
 
-def call_noalloc(builder, plan, x, y):
+class PoolUsage:
+    """High-water mark of the device's default stream-ordered memory pool (the
+    pool cudaMallocAsync draws from), read through the driver API: a call that
+    allocated scratch, even if it freed it again, raises the mark."""
+    USED_MEM_CURRENT, USED_MEM_HIGH = 7, 8   # CUmemPool_attribute
+
+    def __init__(self, dev=0):
+        self.cu = ctypes.CDLL("libcuda.so.1")
+        self.pool = ctypes.c_void_p()
+        assert self.cu.cuDeviceGetDefaultMemPool(ctypes.byref(self.pool), ctypes.c_int(dev)) == 0
+
+    def _get(self, attr):
+        v = ctypes.c_uint64()
+        assert self.cu.cuMemPoolGetAttribute(self.pool, ctypes.c_int(attr), ctypes.byref(v)) == 0
+        return v.value
+
+    def reset(self):
+        zero = ctypes.c_uint64(0)   # resets the high-water mark to the current use
+        assert self.cu.cuMemPoolSetAttribute(self.pool, ctypes.c_int(self.USED_MEM_HIGH), ctypes.byref(zero)) == 0
+        return self._get(self.USED_MEM_CURRENT)
+
+    def high(self):
+        return self._get(self.USED_MEM_HIGH)
+
+
+def call_noalloc(builder, plan, x, y, out=None):
     if builder._swap_operands:
         x, y = y, x
-    out = torch.empty(builder.recipe["out_shape"], dtype=torch.float32, device="cuda")
+    if out is None:
+        out = torch.empty(builder.recipe["out_shape"], dtype=torch.float32, device="cuda")
     rc = lib().pe_contract_noalloc(ctypes.byref(plan), ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(y.data_ptr()),
                                    ctypes.c_void_p(out.data_ptr()),
                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     return rc, out
 
 
-# scratch users: split-K partials (thin output, long K) and gathered operands
+# scratch users: split-K partials (long K, few tiles), the thin kernel's chunk
+# partials (matrix-vector product, 64 chunks per output), gathered operands
 CASES = [("ts, sp -> tp", (512, 8192), (8192, 128), torch.float32),
+         ("ij, j -> i", (64, 1 << 16), (1 << 16,), torch.float32),
          ("bhsc, bcht -> bsht", (2, 8, 16, 20), (2, 20, 8, 24), torch.float16),  # 40-byte rows: gathered
          ("bij, bjk -> bik", (2, 128, 8192), (2, 8192, 96), torch.float16),
          ("ij, jk -> ik", (64, 64), (64, 64), torch.float16)]
@@ -88,12 +116,17 @@ def test_noalloc_matches_pe_contract_twice(eq, s0, s1, dtype):
     run = b.build()
     plan = plan_of(b)
     tol_dtype = dtype
+    pool = PoolUsage(torch.cuda.current_device())
     for k in range(2):  # two calls in a row: the shared array is reused
         x, y = seeded(s0, dtype, 70 + k, "randn").cuda(), seeded(s1, dtype, 80 + k, "randn").cuda()
         ref = run(x, y)
-        rc, out = call_noalloc(b, plan, x, y)
+        out = torch.empty(b.recipe["out_shape"], dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        used = pool.reset()
+        rc, out = call_noalloc(b, plan, x, y, out)
         assert rc == 0, _core.error_string(rc)
         torch.cuda.synchronize()
+        assert pool.high() == used, "pe_contract_noalloc allocated from the stream-ordered pool"
         check_close(out, ref.cpu().numpy(), tol_dtype)
         check_close(out, oracle.einsum_cpu(eq, x.cpu(), y.cpu()), tol_dtype)
     assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
