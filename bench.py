@@ -84,50 +84,90 @@ def metric_of(w):
 
 
 class Clocks:
-    """Sample nvidia-smi clocks / throttle reasons while the benchmark runs."""
+    """Sample the GPU's SM clock and throttle reasons in a background thread
+    (NVML every 2 ms; nvidia-smi every 50 ms where NVML is unavailable), so
+    even a timed region of a few milliseconds gets samples."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, device):
+        self.device = device
+        self.samples = []          # (time, sm MHz, max MHz, set of reason names)
         self.proc = None
-        self.lines = []
+        self.nvml = None
+        self.stop_flag = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
 
     def start(self):
         try:
+            self.nvml = self._nvml_handle()
+        except Exception:
+            self.nvml = None
+        if self.nvml:
+            self.t = threading.Thread(target=self._poll_nvml, daemon=True)
+            self.t.start()
+            return
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+                ["nvidia-smi", f"--id={self.device.index or 0}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read_smi, daemon=True)
             self.t.start()
         except (OSError, ValueError):
             self.proc = None
 
-    def _read(self):
+    def _poll_nvml(self):
+        nv, h = self.nvml
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self.stop_flag.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((time.time(), float(sm), float(mx),
+                                     {n for n, b in zip(self.NAMES, bits) if r & b}))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def _read_smi(self):
         for line in self.proc.stdout:
-            self.lines.append((time.time(), line.strip()))
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[1].replace(".", "").isdigit():
+                continue
+            self.samples.append((time.time(), float(f[1]), float(f[2]) if f[2].replace(".", "").isdigit() else None,
+                                 {self.NAMES[k] for k in range(4) if f[5 + k] == "Active"}))
 
     def summary(self, t0, t1):
         """Median SM clock, max clock and active throttle reasons of the samples
         taken in wall-clock window [t0, t1]."""
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for ts, line in list(self.lines):
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            rows.append((ts, f))
-        inside = [r for r in rows if t0 - 0.05 <= r[0] <= t1 + 0.05] or rows
-        sm = [float(f[1]) for _, f in inside if f[1].replace(".", "").isdigit()]
-        mx = [float(f[2]) for _, f in inside if f[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[k] for _, f in inside for k in range(4) if f[5 + k] == "Active"})
+        if not self.nvml and self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        rows = list(self.samples)
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        if not inside:   # a window shorter than the sampling period: nearest sample
+            inside = sorted(rows, key=lambda r: abs(r[0] - 0.5 * (t0 + t1)))[:1]
+        sm = [r[1] for r in inside]
+        mx = [r[2] for r in inside if r[2]]
+        reasons = sorted(set().union(*[r[3] for r in inside])) if inside else []
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(inside)}
+                "reasons": reasons, "samples": len(inside), "source": "nvml" if self.nvml else "nvidia-smi"}
 
     def stop(self):
+        self.stop_flag.set()
         if self.proc is None:
             return
         self.proc.terminate()
@@ -137,13 +177,17 @@ class Clocks:
             self.proc.kill()
 
 
-def peaks():
+def peaks(sustained=False):
+    """(HBM GB/s, dense bf16 TFLOP/s, source): the driver-measured figures of
+    MEASURED_PEAKS.json (burst GEMM rate, or the rate under the power cap with
+    sustained=True), else this pool's earlier fallback measurement."""
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
-    return 6650.0, 1590.0, "fallback"
+        tf = d.get("bf16_tflops_sustained", 1376.6) if sustained else d.get("bf16_tflops", 1590.0)
+        return d.get("hbm_gbs", 6650.0), tf, "measured" + (" (sustained)" if sustained else " (burst)")
+    return 6650.0, (1400.0 if sustained else 1590.0), "fallback"
 
 
 def traffic_of(name):
@@ -328,6 +372,59 @@ def run_permute_suite(args):
         print(json.dumps({"suite": "permute", "op": "einsum ai,ja->ij (transposed operands)", "n": n,
                           "dtype": str(dt).split(".")[-1], "ms": round(ms, 4), "TFLOP/s": round(2 * n**3 / (ms * 1e-3) / 1e12, 1),
                           "torch_ms": round(mt, 4)}))
+
+
+def run_host_suite(args):
+    """Host cost per runner call: wall time per call of 200 calls submitted while
+    the GPU is held busy by a sleep kernel (so only the host's submit cost is
+    measured, never the GPU's rate), median of 7 samples; for the runner, the bare
+    run_einsum_exec ctypes call, and torch.einsum. Run once more with
+    PE_PLAN_CACHE=0 to see the cost without the prepared-launch cache."""
+    import ctypes
+    from pto_einsum import EinsumBuilder
+    dev = torch.device("cuda", 0)
+    cases = [("ij,jk->ik", (128, 128), (128, 128), torch.float32),
+             ("ij,jk->ik", (128, 128), (128, 128), torch.float16),
+             ("bij,bjk->bik", (8, 128, 128), (8, 128, 128), torch.float16),
+             ("bshd,bthd->bsht", (1, 128, 4, 64), (1, 128, 4, 64), torch.float16),
+             ("ts,ts->ts", (256, 256), (256, 256), torch.float32),
+             ("bsd,d->bsd", (2, 64, 256), (256,), torch.float16)]
+
+    def per_call_us(fn):
+        # the GPU is held busy (torch.cuda._sleep) while the calls are timed, so
+        # the wall time is the host's submit cost alone, never the GPU's rate
+        for _ in range(50):
+            fn()
+        torch.cuda.synchronize()
+        meds = []
+        for _ in range(7):
+            torch.cuda._sleep(200_000_000)
+            t0 = time.perf_counter()
+            for _ in range(200):
+                fn()
+            meds.append((time.perf_counter() - t0) / 200 * 1e6)
+            torch.cuda.synchronize()
+        return statistics.median(meds)
+
+    for eq, s0, s1, dt in cases:
+        a = torch.randn(s0, device=dev).to(dt)
+        b = torch.randn(s1, device=dev).to(dt)
+        bld = EinsumBuilder(eq, [s0, s1], dt)
+        run = bld.build()
+        row = {"suite": "host", "equation": eq, "shape0": s0, "shape1": s1, "dtype": str(dt).split(".")[-1],
+               "cache": os.environ.get("PE_PLAN_CACHE", "1") != "0"}
+        row["runner_us"] = round(per_call_us(lambda: run(a, b)), 2)
+        out = run(a, b)
+        ws = bld.workspace(dev, torch.cuda.current_stream().cuda_stream)
+        st = torch.cuda.current_stream().cuda_stream
+        ex = bld.lib.run_einsum_exec
+        pa, pb, po = a.data_ptr(), b.data_ptr(), out.data_ptr()
+        if bld._swap_operands:
+            pa, pb = pb, pa
+        row["exec_only_us"] = round(per_call_us(lambda: ex(pa, pb, po, ws, st)), 2)
+        row["torch_einsum_us"] = round(per_call_us(lambda: torch.einsum(eq, a, b)), 2)
+        print(json.dumps(row), flush=True)
+        bld.cleanup()
 
 
 def run_thin_suite(args):
@@ -580,18 +677,11 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     for k in range(max(args.warmup, 3)):
         outs[k % nsets] = run(*sets[k % nsets])
     torch.cuda.synchronize(device)
-    # clock window: untimed back-to-back steps before and after the timed region
-    # so the nvidia-smi samples (every 50 ms) see the GPU under this load
-    per_step_s = 1e-3 * max(_time(lambda: run(*sets[0]), 3, 1), 1e-3)
-    roll = max(1, int(0.25 / per_step_s))
-    _barrier(dist, device)
-    t_win0 = time.time()
-    for k in range(roll):
-        outs[k % nsets] = run(*sets[k % nsets])
     _barrier(dist, device)
     launches0 = _core.launch_count()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_win0 = time.time()
     start.record(stream)
     for k in range(steps):
         j = k % nsets
@@ -600,28 +690,48 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
         evs[k][1].record(stream)
     stop.record(stream)
     torch.cuda.synchronize(device)
-    launches = _core.launch_count() - launches0
-    for k in range(roll):
-        outs[k % nsets] = run(*sets[k % nsets])
-    torch.cuda.synchronize(device)
     t_win1 = time.time()
+    launches = _core.launch_count() - launches0
     _barrier(dist, device)
     elapsed_ms = _max_over_ranks(start.elapsed_time(stop), dist, device)
     per_launch_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
     clk = clocks.summary(t_win0, t_win1)
+
+    # Sustained: about one second of back-to-back steps, where the 1 kW power
+    # cap settles the clocks; reported beside the K-step figure.
+    per_step_ms = max(elapsed_ms / steps, 1e-3)
+    n_sus = min(max(steps, int(1000.0 / per_step_ms)), 20000)
+    _barrier(dist, device)
+    s0e, s1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_s0 = time.time()
+    s0e.record(stream)
+    for k in range(n_sus):
+        j = k % nsets
+        outs[j] = run(*sets[j])
+    s1e.record(stream)
+    torch.cuda.synchronize(device)
+    t_s1 = time.time()
+    sus_ms = _max_over_ranks(s0e.elapsed_time(s1e), dist, device)
+    sus_clk = clocks.summary(t_s0 + 0.5 * (t_s1 - t_s0), t_s1)   # second half: settled
     assert _core.device_error(stream.cuda_stream) == 0, "device error word set"
     scale = 1e12 if full["kind"] == "flops" else 1e9
     value = job_units * steps / (elapsed_ms * 1e-3) / scale
+    sus_value = job_units * n_sus / (sus_ms * 1e-3) / scale
 
-    hbm, tflops, peak_src = peaks()
-    if full["bound"] == "tensor":
-        achieved = local["flops"] / (per_launch_ms * 1e-3) / 1e12
-        peak = full.get("tensor_peak", tflops)
-        if peak != tflops:
-            peak_src += " (fp32 3xTF32: bf16 peak / 6)"
-    else:
-        achieved = local["bytes"] / (per_launch_ms * 1e-3) / 1e9
-        peak = hbm
+    def roof(ms_per_launch, sustained):
+        hbm, tflops, src = peaks(sustained)
+        if full["bound"] == "tensor":
+            ach = local["flops"] / (ms_per_launch * 1e-3) / 1e12
+            pk = tflops / (6.0 if dt == "float32" else 1.0)
+            if dt == "float32":
+                src += " (fp32 3xTF32: bf16 peak / 6)"
+        else:
+            ach = local["bytes"] / (ms_per_launch * 1e-3) / 1e9
+            pk = hbm
+        return ach, pk, src
+
+    achieved, peak, peak_src = roof(per_launch_ms, False)
+    s_ach, s_peak, s_src = roof(sus_ms / n_sus, True)
     traffic = traffic_of(name)
     traffic_note = "ncu dram read+write bytes of one full-size launch"
     if traffic is not None and local["units"] != full["units"]:
@@ -636,6 +746,10 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
                         "unit": "TFLOP/s" if full["bound"] == "tensor" else "GB/s",
                         "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
                         "traffic_source": traffic_note, "per_launch_ms": per_launch_ms},
+           "sustained": {"value": sus_value, "steps": n_sus, "ms_per_step": sus_ms / n_sus,
+                         "roofline_frac": s_ach / s_peak, "peak": s_peak, "peak_source": s_src,
+                         "clocks": sus_clk,
+                         "how": "about 1 s of back-to-back steps after the timed region; clocks from its second half"},
            "gpu_launches": launches, "clocks": clk}
 
     if parity and rank == 0:
@@ -716,6 +830,38 @@ def e2e_run(run, a, b, local, job_units, scale, unit, args, dist, device):
             "note": "per rank; value = the job's work per step x steps / max-over-ranks time"}
 
 
+def measure_cpu_path(name, args):
+    """A config on the product's device="cpu" path (config 1 is defined there):
+    wall-clock time of the synchronous host runner, bit-exact parity against the
+    oracle, and the reference's own CPU library timed beside it."""
+    import numpy as np
+    from oracle import oracle
+    from pto_einsum import EinsumBuilder
+    eq, s0, s1, dt = CFG[name]
+    a, b = fullsize.make_inputs(name)
+    bld = EinsumBuilder(eq, [s0, s1], getattr(torch, dt), device="cpu")
+    run = bld.build()
+    for _ in range(3):
+        out = run(a, b)
+    reps = max(args.steps, 10)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        out = run(a, b)
+    dt_s = (time.perf_counter() - t0) / reps
+    w = work(name)
+    metric, unit = metric_of(w)
+    scale = 1e12 if w["kind"] == "flops" else 1e9
+    res = {"device": "cpu (product host path, include/pto_einsum_cpu.h)", "value": w["units"] / dt_s / scale,
+           "unit": unit, "ms_per_step": dt_s * 1e3, "steps": reps, "threads": os.cpu_count(),
+           "parity": {"bit_exact": bool(np.array_equal(out.numpy(), oracle.einsum_cpu(eq, a, b))),
+                      "oracle": "oracle/einsum_oracle.c (restates the reference include/cpu_einsum.h:53-92)"}}
+    r = cpu_reference(name)
+    if r:
+        res["cpu_baseline"] = {"value": r[0], "unit": unit, "cores": r[1], "kind": "reference", "sample": r[2]}
+    bld.cleanup()
+    return res
+
+
 def measure_gather(name, args, rank, world, dist, device):
     """Optional result-on-every-rank path: sharded_einsum(gather=True) (this
     rank's shard, then one NCCL all-gather over NVLink), timed on its own
@@ -759,7 +905,7 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16,
                     help="pipelined end-to-end steps (fill and drain cost about one step)")
-    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin", "host"],
                     help="instead of the one-line benchmark: one JSON line per op of that suite")
     ap.add_argument("--shrink", type=int, default=1,
                     help="divide the config's leading axis (small cases for profiler captures)")
@@ -780,7 +926,7 @@ def main():
         run_reference_arm(args, rank, world)
         return
     suites = {"callers": run_callers_suite, "permute": run_permute_suite, "gdn": run_gdn_suite,
-              "base": run_base_suite, "thin": run_thin_suite}
+              "base": run_base_suite, "thin": run_thin_suite, "host": run_host_suite}
     if args.suite:
         suites[args.suite](args)
         return
@@ -791,7 +937,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=device)
-    clocks = Clocks(local)
+    clocks = Clocks(device)
     clocks.start()
     time.sleep(0.2)
 
@@ -815,6 +961,8 @@ def main():
     for n in others:
         cmap[n] = measure(n, args, rank, world, dist, device, clocks, steps=args.steps, cpu=want_cpu,
                           parity=not args.no_parity)
+    if world == 1 and args.configs != "none":
+        cmap["cfg1"] = measure_cpu_path("cfg1", args)
     clocks.stop()
 
     if rank == 0:

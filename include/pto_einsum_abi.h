@@ -12,8 +12,8 @@
  *
  * Symbol set per route (same as the reference templates):
  *   matmul route       all of the functions below
- *   elementwise route  run_einsum, run_einsum_setup/exec/teardown, run_einsum_last_error
- *   broadcast route    run_einsum, run_einsum_setup/exec/teardown, run_einsum_last_error
+ *   elementwise route  run_einsum, run_einsum_setup/exec/exec_rc/teardown, run_einsum_last_error
+ *   broadcast route    run_einsum, run_einsum_setup/exec/exec_rc/teardown, run_einsum_last_error
  */
 #ifndef PTO_EINSUM_ABI_H
 #define PTO_EINSUM_ABI_H
@@ -42,6 +42,12 @@ void* run_einsum_setup(void* stream);
  * Replaces templates.py:184-186 (einsum_exec, include/pto_einsum.h:253-275). */
 void run_einsum_exec(const void* input0, const void* input1, float* output, void* workspace,
                      void* stream);
+
+/* run_einsum_exec returning the call's status (0 or a pe_status code) instead
+ * of void, so a caller needs one foreign call per contraction (new symbol, no
+ * reference counterpart; run_einsum_exec forwards to it). */
+int run_einsum_exec_rc(const void* input0, const void* input1, float* output, void* workspace,
+                       void* stream);
 
 /* Free the workspace. Replaces templates.py:187-189 (einsum_teardown,
  * include/pto_einsum.h:277-279). */

@@ -103,6 +103,30 @@ int pe_contract(const pe_contract_plan* plan, const void* in0, const void* in1,
  * the device buffer held by the handle.
  */
 void* pe_workspace_create(const pe_contract_plan* plan, void* stream);
+/*
+ * pe_contract with the scratch held by `handle` (pe_workspace_create), the
+ * per-call path of the generated run_einsum_exec (reference einsum_exec,
+ * include/pto_einsum.h:253-275). The handle also remembers the prepared
+ * launches (lowered plan, encoded tensor maps) of its last 8 distinct
+ * (plan, in0, in1, out) combinations, so a repeated call only enqueues its
+ * kernels. Calls on one handle are serialised by a lock.
+ */
+int pe_contract_ws(void* handle, const pe_contract_plan* plan, const void* in0, const void* in1,
+                   float* out, void* stream);
+/*
+ * Phase-gated pe_contract_ws for profiling (the reference's EINSUM_PHASE_STOP
+ * gate, include/pto_einsum.h:18-30, driven by
+ * benchmarks/profile_phase_overlap.py:72-93): the fused kernel keeps its launch
+ * and pipeline-barrier skeleton at every level and runs its work up to
+ *   0 = barriers only, 1 = + operand loads (TMA, gather pre-pass, tf32 split),
+ *   2 = + tensor-core MMAs, 3 = + epilogue stores and split-K reduction (full).
+ * Below 3 the output is not written. Single-phase streaming contractions
+ * (degenerate and thin shapes) launch nothing below 3. A generated library
+ * built with EINSUM_EXTRA_DEFINES="-DEINSUM_PHASE_STOP=N" calls this from its
+ * run_einsum_exec.
+ */
+int pe_contract_ws_phase(void* handle, const pe_contract_plan* plan, const void* in0, const void* in1,
+                         float* out, int phase_stop, void* stream);
 void* pe_workspace_ptr(void* handle);
 size_t pe_workspace_size(void* handle);
 void pe_workspace_destroy(void* handle);

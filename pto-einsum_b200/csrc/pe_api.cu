@@ -26,6 +26,7 @@ struct Workspace {
     void* ptr;
     size_t bytes;
     int device;
+    void* cache;   // prepared launches of recent calls (pe_contract_ws)
 };
 constexpr uint32_t kMagic = 0x50455753u;  // "PEWS"
 }  // namespace
@@ -72,8 +73,23 @@ int pe_contract(const pe_contract_plan* plan, const void* in0, const void* in1, 
     return contract(plan, in0, in1, out, ws, ws_bytes, (cudaStream_t)stream);
 }
 
+int pe_contract_ws(void* handle, const pe_contract_plan* plan, const void* in0, const void* in1, float* out,
+                   void* stream) {
+    Workspace* w = (Workspace*)handle;
+    if (!w || w->magic != kMagic) return set_last_error(PE_ERR_WORKSPACE);
+    return contract_cached(w->cache, plan, in0, in1, out, w->ptr, w->bytes, 3, (cudaStream_t)stream);
+}
+
+int pe_contract_ws_phase(void* handle, const pe_contract_plan* plan, const void* in0, const void* in1,
+                         float* out, int phase_stop, void* stream) {
+    Workspace* w = (Workspace*)handle;
+    if (!w || w->magic != kMagic) return set_last_error(PE_ERR_WORKSPACE);
+    if (phase_stop < 0 || phase_stop > 3) return set_last_error(PE_ERR_INVALID);
+    return contract_cached(w->cache, plan, in0, in1, out, w->ptr, w->bytes, phase_stop, (cudaStream_t)stream);
+}
+
 void* pe_workspace_create(const pe_contract_plan* plan, void* stream) {
-    Workspace* w = new Workspace{kMagic, nullptr, 0, 0};
+    Workspace* w = new Workspace{kMagic, nullptr, 0, 0, program_cache_create()};
     cudaGetDevice(&w->device);
     size_t bytes = 0;
     if (plan && contract_workspace_bytes(plan, &bytes) == PE_OK && bytes > 0) {
@@ -103,6 +119,7 @@ void pe_workspace_destroy(void* handle) {
     Workspace* w = (Workspace*)handle;
     if (!w || w->magic != kMagic) return;
     if (w->ptr) cudaFree(w->ptr);
+    program_cache_destroy(w->cache);
     w->magic = 0;
     delete w;
 }

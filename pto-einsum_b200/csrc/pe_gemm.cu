@@ -27,7 +27,9 @@
 
 #include <algorithm>
 #include <cstring>
+#include <functional>
 #include <mutex>
+#include <vector>
 
 #include <cuda_fp16.h>
 
@@ -69,6 +71,8 @@ struct GemmArgs {
     int sk_q;        // stream-K: k-iterations per CTA (group) over the flattened (tile, k) space; 0 = off
     int nbatch;      // I: batch count of the plan (split-K partials use batch i + sp*I)
     int raw_big;     // fp32: feed x unmasked as the big part (tensor core truncation)
+    int phase;       // phases run (EINSUM_PHASE_STOP): 0 pipeline barriers only, 1 + operand
+                     // loads, 2 + tensor-core MMAs, 3 + epilogue stores (the full kernel)
     float* out;
     Decode ob, om, on;
 };
@@ -258,6 +262,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     // pairs: the leader's barrier counts both CTAs' bytes
                     int tx = C::TX_BYTES * (C::PAIR ? 2 : 1);
                     if constexpr (C::F32) tx += (g.a_pre ? C::A_BYTES : 0) + (g.b_pre ? C::B_BYTES : 0);
+                    if (g.phase < 1) {
+                        // phase gate: the stage completes without data
+                        if (rank == 0) mbar_arrive(full(stage));
+                        if (++stage == C::STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                        continue;
+                    }
                     if (rank == 0) mbar_arrive_expect_tx(full(stage), tx);
                     issued_mask |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -337,6 +350,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     const uint32_t d = dbuf + (uint32_t)(slot * C::BN);
 #pragma unroll
                     for (int ks = 0; ks < C::KSUB; ++ks) {
+                        if (g.phase < 2) break;  // phase gate: no MMAs
                         const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, b_sbo, b_lay);
                         const uint32_t accum = (kb - kb_lo >= S || ks > 0) ? 1u : 0u;
@@ -469,24 +483,25 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             // Two register buffers: the TMEM load of the next chunk is in flight
             // while the current one is written out.
             uint32_t va[32], vb[32];
-            if (half < nvalid) {
+            const int nv = g.phase >= 3 ? nvalid : 0;  // phase gate: no TMEM reads or stores
+            if (half < nv) {
                 __syncwarp();
                 tmem_ld32(tbase + half * 32, va);
                 tmem_ld_wait();
             }
 #pragma unroll 1
-            for (int c = half; c < nvalid; c += 2 * NH) {
+            for (int c = half; c < nv; c += 2 * NH) {
                 const int c1 = c + NH, c2 = c + 2 * NH;
                 __syncwarp();
-                if (c1 < nvalid) tmem_ld32(tbase + c1 * 32, vb);
+                if (c1 < nv) tmem_ld32(tbase + c1 * 32, vb);
                 emit(va, c);
-                if (c1 >= nvalid) break;
+                if (c1 >= nv) break;
                 __syncwarp();
                 tmem_ld_wait();
-                if (c2 < nvalid) tmem_ld32(tbase + c2 * 32, va);
+                if (c2 < nv) tmem_ld32(tbase + c2 * 32, va);
                 emit(vb, c1);
                 __syncwarp();
-                if (c2 < nvalid) tmem_ld_wait();
+                if (c2 < nv) tmem_ld_wait();
             }
             tc_fence_before();
             __syncwarp();
@@ -1593,8 +1608,19 @@ OperandView canonical_view(const void* base, int64_t I, int64_t L, int64_t C, in
     return v;
 }
 
-int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
-                     float* out, void* ws, cudaStream_t s);
+// The launches of one contraction, prepared on the host (plan lowered, tensor
+// maps encoded) and replayable: each step enqueues one kernel on the stream.
+using Step = std::function<int(cudaStream_t)>;
+using Program = std::vector<Step>;
+
+int build_program(const pe_contract_plan& pl, const Lowered& L, const void* in0, const void* in1,
+                  float* out, void* ws, int phase, Program& prog);
+
+int run_program(const Program& prog, cudaStream_t s) {
+    for (const Step& st : prog)
+        if (int rc = st(s)) return rc;
+    return set_last_error(PE_OK);
+}
 
 }  // namespace
 
@@ -1618,54 +1644,160 @@ int contract_scratch_bytes(const pe_contract_plan* plan, const void* in0, const 
     return set_last_error(PE_OK);
 }
 
-int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
-             size_t ws_bytes, cudaStream_t s) {
+namespace {
+
+// Lower the plan for these pointers and build its launch program. `tmp_bytes`
+// > 0 means the caller's workspace is too small for this call (a misaligned
+// view needs a gather the plan-time size did not include).
+int prepare(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
+            size_t ws_bytes, int phase, Program& prog, size_t* tmp_bytes) {
+    *tmp_bytes = 0;
     Lowered L;
     int rc = lower(pl, in0, in1, &L);
     if (rc) return set_last_error(rc);
     const int64_t n_out = pl->I * pl->L0 * pl->L1;
     if (n_out == 0) return set_last_error(PE_OK);
     if (!out) return set_last_error(PE_ERR_INVALID);
-    if (pl->C == 0) return check_cuda(cudaMemsetAsync(out, 0, (size_t)n_out * 4, s));
+    if (pl->C == 0) {
+        const size_t nb = (size_t)n_out * 4;
+        if (phase < 3) return set_last_error(PE_OK);
+        prog.push_back([out, nb](cudaStream_t s) { return check_cuda(cudaMemsetAsync(out, 0, nb, s)); });
+        return set_last_error(PE_OK);
+    }
     if (!in0 || !in1) return set_last_error(PE_ERR_INVALID);
-    if (L.simt) return small_contract_launch(pl, L, in0, in1, out, s);
-    if (!get_encode()) return set_last_error(PE_ERR_NO_DEVICE);
-    void* tmp_ws = nullptr;
+    if (!L.simt && !get_encode()) return set_last_error(PE_ERR_NO_DEVICE);
     if (L.ws_bytes > 0 && (!ws || ws_bytes < L.ws_bytes)) {
-        // The plan-time size assumed 16-byte aligned inputs; a misaligned view
-        // needs a gather the caller did not budget for: take stream-ordered
-        // scratch for this call only.
-        rc = check_cuda(cudaMallocAsync(&tmp_ws, L.ws_bytes, s));
-        if (rc) return rc;
-        ws = tmp_ws;
+        *tmp_bytes = L.ws_bytes;
+        return set_last_error(PE_OK);
     }
-    rc = contract_lowered(pl, L, in0, in1, out, ws, s);
-    if (tmp_ws) {
-        int rc2 = check_cuda(cudaFreeAsync(tmp_ws, s));
-        if (!rc) rc = rc2;
+    return build_program(*pl, L, in0, in1, out, ws, phase, prog);
+}
+
+// Per-workspace-handle cache of prepared programs, keyed by the exact
+// pointers of the call: a repeat call replays its launches without lowering
+// the plan or encoding tensor maps again.
+struct CacheEntry {
+    const pe_contract_plan* plan = nullptr;
+    pe_contract_plan plan_copy;
+    int phase = 3;
+    const void* in0 = nullptr;
+    const void* in1 = nullptr;
+    float* out = nullptr;
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    uint64_t used = 0;
+    Program prog;
+};
+
+struct ProgramCache {
+    static constexpr int kEntries = 8;
+    std::mutex mu;
+    CacheEntry e[kEntries];
+    uint64_t clock = 0;
+};
+
+}  // namespace
+
+int contract_phase(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
+                   size_t ws_bytes, int phase, cudaStream_t s) {
+    Program prog;
+    size_t tmp_bytes = 0;
+    int rc = prepare(pl, in0, in1, out, ws, ws_bytes, phase, prog, &tmp_bytes);
+    if (rc) return rc;
+    if (tmp_bytes == 0) return run_program(prog, s);
+    // stream-ordered scratch for this call only
+    void* tmp_ws = nullptr;
+    rc = check_cuda(cudaMallocAsync(&tmp_ws, tmp_bytes, s));
+    if (rc) return rc;
+    rc = prepare(pl, in0, in1, out, tmp_ws, tmp_bytes, phase, prog, &tmp_bytes);
+    if (!rc) rc = run_program(prog, s);
+    int rc2 = check_cuda(cudaFreeAsync(tmp_ws, s));
+    return rc ? rc : rc2;
+}
+
+int contract(const pe_contract_plan* pl, const void* in0, const void* in1, float* out, void* ws,
+             size_t ws_bytes, cudaStream_t s) {
+    return contract_phase(pl, in0, in1, out, ws, ws_bytes, 3, s);
+}
+
+void* program_cache_create() { return new ProgramCache(); }
+
+void program_cache_destroy(void* c) { delete (ProgramCache*)c; }
+
+int contract_cached(void* cache, const pe_contract_plan* pl, const void* in0, const void* in1, float* out,
+                    void* ws, size_t ws_bytes, int phase, cudaStream_t s) {
+    ProgramCache* pc = (ProgramCache*)cache;
+    // PE_PLAN_CACHE=0 turns the cache off (every call lowers and encodes again)
+    static const bool enabled = [] {
+        const char* e = getenv("PE_PLAN_CACHE");
+        return !(e && e[0] == '0');
+    }();
+    if (!pc || !pl || !enabled) return contract_phase(pl, in0, in1, out, ws, ws_bytes, phase, s);
+    std::lock_guard<std::mutex> lk(pc->mu);
+    CacheEntry* victim = &pc->e[0];
+    for (CacheEntry& e : pc->e) {
+        if (e.plan == pl && e.phase == phase && e.in0 == in0 && e.in1 == in1 && e.out == out && e.ws == ws &&
+            e.ws_bytes == ws_bytes && memcmp(&e.plan_copy, pl, sizeof(*pl)) == 0) {
+            e.used = ++pc->clock;
+            return run_program(e.prog, s);
+        }
+        if (e.used < victim->used) victim = &e;
     }
+    Program prog;
+    size_t tmp_bytes = 0;
+    int rc = prepare(pl, in0, in1, out, ws, ws_bytes, phase, prog, &tmp_bytes);
+    if (rc) return rc;
+    if (tmp_bytes) return contract_phase(pl, in0, in1, out, ws, ws_bytes, phase, s);  // not cached
+    rc = run_program(prog, s);
+    if (rc) return rc;
+    victim->plan = pl;
+    victim->plan_copy = *pl;
+    victim->phase = phase;
+    victim->in0 = in0;
+    victim->in1 = in1;
+    victim->out = out;
+    victim->ws = ws;
+    victim->ws_bytes = ws_bytes;
+    victim->used = ++pc->clock;
+    victim->prog = std::move(prog);
     return rc;
 }
 
 namespace {
-int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* in0, const void* in1,
-                     float* out, void* ws, cudaStream_t s) {
-    if (L.thin) return thin_contract_launch(pl, L, in0, in1, out, ws, s);
+int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in0, const void* in1,
+                  float* out, void* ws, int phase, Program& prog) {
+    const pe_contract_plan* pl = &plan;
+    // phase gate (EINSUM_PHASE_STOP): the single-phase streaming kernels run only
+    // in full builds; the fused GEMM keeps its barrier skeleton at every level
+    if ((L.simt || L.thin) && phase < 3) return set_last_error(PE_OK);
+    if (L.simt) {
+        prog.push_back([plan, L, in0, in1, out](cudaStream_t s) {
+            return small_contract_launch(&plan, L, in0, in1, out, s);
+        });
+        return set_last_error(PE_OK);
+    }
+    if (L.thin) {
+        prog.push_back([plan, L, in0, in1, out, ws](cudaStream_t s) {
+            return thin_contract_launch(&plan, L, in0, in1, out, ws, s);
+        });
+        return set_last_error(PE_OK);
+    }
     const int es = pl->dtype == PE_F32 ? 4 : 2;
-    int rc = PE_OK;
     OperandView va = L.a, vb = L.b;
     if (L.a_ws) {
         void* dst = (uint8_t*)ws + L.a_off;
-        rc = gather_canonical(es, in0, dst, L.a_batch, L.nb, L.a_free, L.n0, L.a_ct, L.nc, pl->L0,
-                              L.kpad, s);
-        if (rc) return rc;
+        const int64_t L0 = pl->L0, kpad = L.kpad;
+        if (phase >= 1) prog.push_back([es, in0, dst, L, L0, kpad](cudaStream_t s) {
+            return gather_canonical(es, in0, dst, L.a_batch, L.nb, L.a_free, L.n0, L.a_ct, L.nc, L0, kpad, s);
+        });
         va = canonical_view(dst, pl->I, pl->L0, pl->C, L.kpad);
     }
     if (L.b_ws) {
         void* dst = (uint8_t*)ws + L.b_off;
-        rc = gather_canonical(es, in1, dst, L.b_batch, L.nb, L.b_free, L.n1, L.b_ct, L.nc, pl->L1,
-                              L.kpad, s);
-        if (rc) return rc;
+        const int64_t L1 = pl->L1, kpad = L.kpad;
+        if (phase >= 1) prog.push_back([es, in1, dst, L, L1, kpad](cudaStream_t s) {
+            return gather_canonical(es, in1, dst, L.b_batch, L.nb, L.b_free, L.n1, L.b_ct, L.nc, L1, kpad, s);
+        });
         vb = canonical_view(dst, pl->I, pl->L1, pl->C, L.kpad);
     }
     GemmArgs g;
@@ -1681,6 +1813,7 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     g.sk_q = (int)L.sk_q;
     g.nbatch = (int)pl->I;
     g.raw_big = raw_big_enabled();
+    g.phase = phase;
     OutView slab;  // split-K: canonical partial slabs [ksplit * I, L0, L1]
     const OutView* ov = &L.out;
     float* target = out;
@@ -1698,6 +1831,14 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
     g.om = make_decode(ov->m, ov->nm);
     g.on = make_decode(ov->n, ov->nn);
     g.tiles = (int)pl->I;
+    // the GEMM step launches a copy: launch_gemm fills in the tile counts
+    auto gemm_step = [&prog](auto cfg_tag, const GemmArgs& ga) {
+        using C = decltype(cfg_tag);
+        prog.push_back([ga](cudaStream_t s) {
+            GemmArgs gg = ga;
+            return launch_gemm<C>(gg, s);
+        });
+    };
     const bool f32 = pl->dtype == PE_F32;
     if (f32) {
         // more slots for long contractions: fewer accumulation steps per slot
@@ -1720,8 +1861,7 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
             if (!encode_operand(&g.tmbs, v, true, 128)) return set_last_error(PE_ERR_UNSUPPORTED);
             g.b_pre = 1;
         }
-        rc = tf32_small_launch(ra, rb, s);
-        if (rc) return rc;
+        if ((ra.n || rb.n) && phase >= 1) prog.push_back([ra, rb](cudaStream_t s) { return tf32_small_launch(ra, rb, s); });
         if (!encode_operand(&g.tma, va, true, 128) || !encode_operand(&g.tmb, vb, true, 128))
             return set_last_error(PE_ERR_UNSUPPORTED);
         // both small halves precomputed: the split warps have nothing to do, so
@@ -1734,11 +1874,11 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
             vbs.base = (uint8_t*)ws + L.bs_off;
             if (!encode_operand(&g.tmb, vb, true, 256) || !encode_operand(&g.tmbs, vbs, true, 256))
                 return set_last_error(PE_ERR_UNSUPPORTED);
-            rc = launch_gemm<Cfg<256, true, 8, false, 0>>(g, s);
+            gemm_step(Cfg<256, true, 8, false, 0>{}, g);
         } else if (g.a_pre && g.b_pre) {
-            rc = launch_gemm<Cfg<128, true, 8, false, 0>>(g, s);
+            gemm_step(Cfg<128, true, 8, false, 0>{}, g);
         } else {
-            rc = launch_gemm<Cfg<128, true>>(g, s);
+            gemm_step(Cfg<128, true>{}, g);
         }
     } else {
         // pairs halve each SM's operand traffic, which pays off where the
@@ -1747,13 +1887,35 @@ int contract_lowered(const pe_contract_plan* pl, const Lowered& L, const void* i
         if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, pair ? 128 : L.bn))
             return set_last_error(PE_ERR_UNSUPPORTED);
         if (pair)
-            rc = launch_gemm<Cfg<256, false, 8, true>>(g, s);
+            gemm_step(Cfg<256, false, 8, true>{}, g);
+        else if (L.bn == 256)
+            gemm_step(Cfg<256, false>{}, g);
         else
-            rc = L.bn == 256 ? launch_gemm<Cfg<256, false>>(g, s) : launch_gemm<Cfg<128, false>>(g, s);
+            gemm_step(Cfg<128, false>{}, g);
     }
-    if (rc || L.ksplit <= 1) return rc;
-    if (L.sk_q > 0) return streamk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g, s);
-    return splitk_reduce_launch((const float*)((uint8_t*)ws + L.p_off), out, L, pl, g.ksplit, s);
+    if (L.ksplit <= 1 || phase < 3) return set_last_error(PE_OK);
+    const float* part = (const float*)((uint8_t*)ws + L.p_off);
+    if (L.sk_q > 0) {
+        GemmArgs gk = g;  // the reduction needs the k-iteration count of the GEMM
+        gk.kiters = (int)((g.K + 128 / es - 1) / (128 / es));
+        prog.push_back([part, out, L, plan, gk](cudaStream_t s) {
+            return streamk_reduce_launch(part, out, L, &plan, gk, s);
+        });
+    } else {
+        // launch_gemm rounds ksplit so that every unit gets >= 1 k-iteration
+        const int kiters = (int)((g.K + 128 / es - 1) / (128 / es));
+        int ks = g.ksplit;
+        if (ks > 1 && kiters >= 2) {
+            const int kper = (kiters + ks - 1) / ks;
+            ks = (kiters + kper - 1) / kper;
+        } else {
+            ks = 1;
+        }
+        prog.push_back([part, out, L, plan, ks](cudaStream_t s) {
+            return splitk_reduce_launch(part, out, L, &plan, ks, s);
+        });
+    }
+    return set_last_error(PE_OK);
 }
 
 }  // namespace

@@ -29,6 +29,14 @@ int contract_scratch_bytes(const pe_contract_plan* plan, const void* in0, const 
 int contract(const pe_contract_plan* plan, const void* in0, const void* in1, float* out, void* ws,
              size_t ws_bytes, cudaStream_t s);
 
+// Prepared-launch cache held by a workspace handle: contract_cached replays the
+// launches of an earlier call with the same plan object and pointers.
+void* program_cache_create();
+void program_cache_destroy(void* cache);
+// phase: EINSUM_PHASE_STOP level (3 = the full contraction)
+int contract_cached(void* cache, const pe_contract_plan* plan, const void* in0, const void* in1, float* out,
+                    void* ws, size_t ws_bytes, int phase, cudaStream_t s);
+
 // Read (and optionally clear) the device error word of the GEMM kernels.
 int gemm_device_error(bool clear);
 int wait_timeout_selftest(uint64_t timeout_ns, cudaStream_t s);

@@ -59,6 +59,15 @@ def _cuda_device(device) -> torch.device:
     return dev
 
 
+def _raw_stream_getter():
+    """Function device index -> current CUDA stream handle (int). torch's own
+    accessor avoids building a Stream object per call where it exists."""
+    f = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if f is not None:
+        return f
+    return lambda idx: torch.cuda.current_stream(idx).cuda_stream
+
+
 class EinsumBuilder:
     """Plan, compile (with caching) and run one two-operand einsum on a B200."""
 
@@ -346,6 +355,9 @@ class EinsumBuilder:
         # ctypes pointer objects on every call; pointer instances are accepted too
         self.lib.run_einsum_exec.argtypes = [ctypes.c_void_p] * 5
         self.lib.run_einsum_exec.restype = None
+        # same call returning its status (one foreign call per runner call)
+        self.lib.run_einsum_exec_rc.argtypes = [ctypes.c_void_p] * 5
+        self.lib.run_einsum_exec_rc.restype = ctypes.c_int
         self.lib.run_einsum_teardown.argtypes = [ctypes.c_void_p]
         self.lib.run_einsum_teardown.restype = None
         self.lib.run_einsum_last_error.argtypes = []
@@ -387,8 +399,11 @@ class EinsumBuilder:
         swap = self._swap_operands
         if self._plan_device == "cpu":
             return self._cpu_runner(shapes, out_shape)
-        exec_fn = self.lib.run_einsum_exec
-        last_error = self.lib.run_einsum_last_error
+        exec_rc = self.lib.run_einsum_exec_rc
+        raw_stream = _raw_stream_getter()
+        get_device = torch._C._cuda_getDevice if hasattr(torch._C, "_cuda_getDevice") else torch.cuda.current_device
+        f32 = torch.float32
+        empty = torch.empty
 
         def run(*operands):
             if len(operands) != 2:
@@ -410,29 +425,30 @@ class EinsumBuilder:
                 inp1 = inp1.contiguous()
             if swap:
                 inp0, inp1 = inp1, inp0
-            out = torch.empty(out_shape, dtype=torch.float32, device=dev)
-            if out.numel() == 0:
+            out = empty(out_shape, dtype=f32, device=dev)
+            if empty_out:
                 return out
             if self.lib is None:
                 raise RuntimeError("pto_einsum: runner called after cleanup()")
             idx = dev.index
             wss = self._workspace
             ws = wss.get(idx) if wss else None
-            if idx == torch.cuda.current_device():
-                stream = torch.cuda.current_stream().cuda_stream
+            if idx == get_device():
+                stream = raw_stream(idx)
                 if ws is None:
                     ws = self.workspace(dev, stream)
-                exec_fn(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
+                rc = exec_rc(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
             else:
                 stream = torch.cuda.current_stream(dev).cuda_stream
                 if ws is None:
                     ws = self.workspace(dev, stream)
                 with torch.cuda.device(dev):
-                    exec_fn(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
-            if last_error():
+                    rc = exec_rc(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), ws, stream)
+            if rc:
                 self._check("run_einsum_exec")
             return out
 
+        empty_out = prod(out_shape) == 0
         return run
 
     def _cpu_runner(self, shapes, out_shape):

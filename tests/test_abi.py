@@ -49,7 +49,8 @@ def test_generated_library_exports(eq, shapes, route, dtype):
     b.load_library()
     syms = exported(b.so_filename)
     abi = declared("pto_einsum_abi.h")
-    need = {"run_einsum", "run_einsum_setup", "run_einsum_exec", "run_einsum_teardown", "run_einsum_last_error"}
+    need = {"run_einsum", "run_einsum_setup", "run_einsum_exec", "run_einsum_exec_rc", "run_einsum_teardown",
+            "run_einsum_last_error"}
     if route == "matmul":
         need = abi
     assert need <= abi
@@ -75,13 +76,31 @@ def test_cache_and_cleanup():
     assert not os.path.exists(b.target_dir)
 
 
-def test_extra_defines_tag(monkeypatch):
+def _undefined_symbols(so):
+    out = subprocess.run(["nm", "-D", "--undefined-only", so], capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+@pytest.mark.parametrize("stop", [None, 0, 1, 2, 3])
+def test_extra_defines_phase_stop_reaches_the_core(monkeypatch, stop):
+    """EINSUM_EXTRA_DEFINES carries -DEINSUM_PHASE_STOP=N into the generated
+    library (reference builder.py:691-700, profile_phase_overlap.py:72-93): the
+    cached file name gets a define tag and, below 3, run_einsum_exec calls the
+    phase-gated core entry point instead of the ordinary one."""
+    if stop is not None:
+        monkeypatch.setenv("EINSUM_EXTRA_DEFINES", f"-DEINSUM_PHASE_STOP={stop}")
+    else:
+        monkeypatch.delenv("EINSUM_EXTRA_DEFINES", raising=False)
     b = EinsumBuilder("ij,jk->ik", [(16, 32), (32, 16)], torch.float32)
     b.parse_equation()
     b.generate_code()
-    monkeypatch.setenv("EINSUM_EXTRA_DEFINES", "-DEINSUM_PHASE_STOP=1")
     b.compile()
-    assert re.search(r"einsum_[0-9a-f]{32}_[0-9a-f]{8}\.so$", b.so_filename)
+    tagged = re.search(r"einsum_[0-9a-f]{32}_[0-9a-f]{8}\.so$", b.so_filename)
+    assert bool(tagged) == (stop is not None)
+    syms = _undefined_symbols(b.so_filename)
+    gated = stop is not None and stop < 3
+    assert ("pe_contract_ws_phase" in syms) == gated
+    assert ("pe_contract_ws" in syms) == (not gated)
     b.cleanup()
 
 
