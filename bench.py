@@ -427,6 +427,38 @@ def run_host_suite(args):
         bld.cleanup()
 
 
+def run_phases_suite(args):
+    """The reference's phase-overlap study (benchmarks/profile_phase_overlap.py:72-128)
+    on the fused kernel: each config built with EINSUM_PHASE_STOP = 0 (launch and
+    pipeline barriers), 1 (+ operand loads), 2 (+ tensor-core MMAs), 3 (+ epilogue
+    stores: the full kernel); CUDA-event time per call, the per-phase increments by
+    subtraction. Contraction configs only (--configs selects)."""
+    from pto_einsum import EinsumBuilder
+    dev = torch.device("cuda", 0)
+    names = [n for n in CFG if n not in ("cfg1",) and n not in fullsize.EXACT]
+    if args.configs not in ("all", "none"):
+        names = [n for n in args.configs.split(",") if n]
+    steps = max(args.steps // 4, 20)
+    for name in names:
+        eq, s0, s1, dt = CFG[name]
+        a, b = fullsize.make_inputs(name, device=dev)
+        row = {"suite": "phases", "config": name, "equation": eq}
+        for stop in (0, 1, 2, 3):
+            os.environ["EINSUM_EXTRA_DEFINES"] = f"-DEINSUM_PHASE_STOP={stop}"
+            bld = EinsumBuilder(eq, [s0, s1], getattr(torch, dt))
+            run = bld.build()
+            row[f"stop{stop}_us"] = round(_time(lambda: run(a, b), steps, 3) * 1e3, 2)
+            bld.cleanup()
+        os.environ.pop("EINSUM_EXTRA_DEFINES", None)
+        row["barriers_us"] = row["stop0_us"]
+        row["loads_us"] = round(row["stop1_us"] - row["stop0_us"], 2)
+        row["mma_us"] = round(row["stop2_us"] - row["stop1_us"], 2)
+        row["epilogue_us"] = round(row["stop3_us"] - row["stop2_us"], 2)
+        print(json.dumps(row), flush=True)
+        del a, b
+        torch.cuda.empty_cache()
+
+
 def run_thin_suite(args):
     """Thin outputs and few-tile long contractions: dot and matrix-vector products
     (streaming thin-output kernel) and thin GEMMs (stream-K), each vs torch.einsum,
@@ -700,7 +732,7 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     # Sustained: about one second of back-to-back steps, where the 1 kW power
     # cap settles the clocks; reported beside the K-step figure.
     per_step_ms = max(elapsed_ms / steps, 1e-3)
-    n_sus = min(max(steps, int(1000.0 / per_step_ms)), 20000)
+    n_sus = min(max(steps, int(args.sustained_ms / per_step_ms)), 20000) if args.sustained_ms > 0 else steps
     _barrier(dist, device)
     s0e, s1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_s0 = time.time()
@@ -905,8 +937,10 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16,
                     help="pipelined end-to-end steps (fill and drain cost about one step)")
-    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin", "host"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin", "host", "phases"],
                     help="instead of the one-line benchmark: one JSON line per op of that suite")
+    ap.add_argument("--sustained-ms", type=float, default=1000.0,
+                    help="length of the sustained back-to-back run after the timed region (0: K steps only)")
     ap.add_argument("--shrink", type=int, default=1,
                     help="divide the config's leading axis (small cases for profiler captures)")
     args = ap.parse_args()
@@ -926,7 +960,8 @@ def main():
         run_reference_arm(args, rank, world)
         return
     suites = {"callers": run_callers_suite, "permute": run_permute_suite, "gdn": run_gdn_suite,
-              "base": run_base_suite, "thin": run_thin_suite, "host": run_host_suite}
+              "base": run_base_suite, "thin": run_thin_suite, "host": run_host_suite,
+              "phases": run_phases_suite}
     if args.suite:
         suites[args.suite](args)
         return
@@ -935,6 +970,10 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     if world > 1:
+        # one kernel cache per rank: ranks build the same libraries and clean up
+        # after themselves
+        base = os.environ.get("EINSUM_BUILD_DIR") or os.path.join(os.getcwd(), "build")
+        os.environ["EINSUM_BUILD_DIR"] = os.path.join(base, f"rank{rank}")
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=device)
     clocks = Clocks(device)
@@ -977,6 +1016,7 @@ def main():
                                        "(pto_einsum.distributed.shard_operands), no collective on the data path"),
             "roofline": head["roofline"], "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"],
             "parity": head.get("parity"), "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+            "sustained": head["sustained"],
         }
         line.update(extra)
         if cmap:

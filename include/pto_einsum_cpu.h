@@ -70,11 +70,17 @@ inline void parallel_rows(int64_t rows, int64_t work_per_row, F f) {
     }
     std::vector<std::thread> th;
     const int64_t per = (rows + nt - 1) / nt;
-    for (int64_t t = 0; t < nt; ++t) {
+    int64_t t = 0;
+    for (; t < nt; ++t) {
         const int64_t lo = t * per, hi = std::min(rows, lo + per);
         if (lo >= hi) break;
-        th.emplace_back([=, &f] { f(lo, hi); });
+        try {
+            th.emplace_back([=, &f] { f(lo, hi); });
+        } catch (...) {
+            break;  // no thread could be started (resource limits): finish here
+        }
     }
+    if (t * per < rows) f(t * per, rows);
     for (auto& x : th) x.join();
 }
 
@@ -91,7 +97,7 @@ inline int einsum(const T* data0, const T* data1, float* res) {
         b.resize((size_t)P1::N);
         o.resize((size_t)PO::N);
     } catch (...) {
-        return 1;
+        return 1;  // host memory exhausted: reported, nothing written
     }
     for_each_perm<P0>([&](int64_t d, int64_t s) { a[(size_t)d] = static_cast<float>(data0[s]); });
     for_each_perm<P1>([&](int64_t d, int64_t s) { b[(size_t)d] = static_cast<float>(data1[s]); });

@@ -97,6 +97,9 @@ void* pe_workspace_create(const pe_contract_plan* plan, void* stream) {
             w->bytes = bytes;
             set_last_error(PE_OK);
         } else {
+            // not sticky: clear the runtime's last-error slot so later launch
+            // checks on this thread do not report this failure again
+            (void)cudaGetLastError();
             w->ptr = nullptr;
             set_last_error(PE_ERR_CUDA);
         }

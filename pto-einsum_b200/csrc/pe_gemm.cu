@@ -14,9 +14,10 @@
 //    into a STAGES-deep shared-memory ring, one thread of warp 1 issues
 //    tcgen05.mma into a double-buffered TMEM accumulator, warps 2-5 drain the
 //    other accumulator while the next tile is multiplied.
-//  * Phase C (output permute) is fused into the epilogue: tcgen05.ld -> 128B
-//    swizzled staging -> TMA store through a tensor map over the permuted
-//    output, or, when no tensor map fits, strided global stores.
+//  * Phase C (output permute) is fused into the epilogue: tcgen05.ld in the
+//    16x256b layout -> full-sector 8-byte stores into the permuted output when
+//    its rows are unit-stride (16-byte aligned strides), else strided stores
+//    decoded per row and column.
 //  fp16 operands use kind::f16 with fp32 accumulation. fp32 operands use
 //  kind::tf32 in the 3xTF32 scheme: x = big + small with big = x with the low
 //  13 mantissa bits cleared (exactly representable in tf32) and small = x - big;
@@ -56,15 +57,14 @@ struct Decode {
 struct GemmArgs {
     CUtensorMap tma;
     CUtensorMap tmb;
-    CUtensorMap tmc;
     CUtensorMap tmas;   // fp32: precomputed tf32 "small" halves of A / B (same layout)
     CUtensorMap tmbs;
     int a_pre, b_pre;   // fp32: operand's small half comes from tmas / tmbs
     int M, N, K;
     int mblk, nblk, tiles, kiters;
     int a_mn, b_mn;
-    MapBatch ab, bb, cb;
-    int out_tma;
+    MapBatch ab, bb;
+    int out_rows;    // output rows unit-stride with 16-byte aligned strides (full-sector stores)
     int acc_slots;   // fp32: accumulator slots per tile (1, 2 or 4)
     int ksplit;      // work units per output tile (split-K), >= 1
     int kper;        // k-iterations per unit
@@ -94,14 +94,12 @@ struct Cfg {
     static constexpr int B_BYTES = BNL * 128;
     static constexpr int TX_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
-    // epilogue warps (two per TMEM lane quadrant for fp16), 2 x 4 KB staging each
     // epilogue warps: 4 (one per TMEM lane quadrant) or more, sharing quadrants
     // by alternating 32-column chunks; more warps raise the output rate of
-    // store-bound shapes, fewer leave shared memory for pipeline stages
+    // store-bound shapes. The epilogue uses no shared memory, so the operand
+    // ring takes the whole 224 KB budget.
     static constexpr int EPIW = EPIW_;
-    static constexpr int EBUF = 1;   // one 4 KB transpose buffer per epilogue warp
-    static constexpr int EPI_BYTES = EPIW * EBUF * 4096;
-    static constexpr int STAGES = (224 * 1024 - EPI_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = (224 * 1024) / STAGE_BYTES;
     static constexpr int UMMA_K = F32 ? 8 : 16;
     static constexpr int KSUB = BK / UMMA_K;
     // fp32: each accumulator buffer holds two BN-column sums (big*big and the
@@ -117,10 +115,11 @@ struct Cfg {
     static constexpr int SPLITW = SPLITW_;
     static constexpr int THREADS = 64 + 32 * EPIW + 32 * SPLITW;
     static constexpr int NBARS = 3 * STAGES + 9;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + NBARS * 8 + 16;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + NBARS * 8 + 16;
     static_assert(SMEM <= 232448, "shared memory budget");
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
-    static_assert(!PAIR || !F32, "CTA pairs are fp16-only");
+    // fp32 pairs only with both tf32 small halves precomputed (no split warps)
+    static_assert(!PAIR || !F32 || SPLITW == 0, "fp32 CTA pairs need precomputed small halves");
 };
 
 // Batch coordinates of flat batch index i in one map (fully unrolled so the
@@ -187,8 +186,7 @@ template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* epi = smem + C::STAGES * C::STAGE_BYTES;
-    uint64_t* bars = (uint64_t*)(epi + C::EPI_BYTES);
+    uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
     uint32_t* tmem_slot = (uint32_t*)(bars + C::NBARS);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
@@ -222,7 +220,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         fence_barrier_init();
         tma_prefetch(&g.tma);
         tma_prefetch(&g.tmb);
-        if (g.out_tma) tma_prefetch(&g.tmc);
     }
     if (warp == 1) {
         if constexpr (C::PAIR) {
@@ -260,8 +257,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     uint8_t* sb = sa + C::A_BYTES;
                     const int k0 = kb * C::BK;
                     // pairs: the leader's barrier counts both CTAs' bytes
-                    int tx = C::TX_BYTES * (C::PAIR ? 2 : 1);
+                    int tx = C::TX_BYTES;
                     if constexpr (C::F32) tx += (g.a_pre ? C::A_BYTES : 0) + (g.b_pre ? C::B_BYTES : 0);
+                    if constexpr (C::PAIR) tx *= 2;
                     if (g.phase < 1) {
                         // phase gate: the stage completes without data
                         if (rank == 0) mbar_arrive(full(stage));
@@ -357,9 +355,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         if constexpr (C::F32) {
                             const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                            mma_tf32(d, ads, bd, idesc, accum);
-                            mma_tf32(d, ad, bds, idesc, 1u);
-                            mma_tf32(d, ad, bd, idesc, 1u);
+                            if constexpr (C::PAIR) {
+                                mma_tf32_pair(d, ads, bd, idesc, accum);
+                                mma_tf32_pair(d, ad, bds, idesc, 1u);
+                                mma_tf32_pair(d, ad, bd, idesc, 1u);
+                            } else {
+                                mma_tf32(d, ads, bd, idesc, accum);
+                                mma_tf32(d, ad, bds, idesc, 1u);
+                                mma_tf32(d, ad, bd, idesc, 1u);
+                            }
                         } else if constexpr (C::PAIR) {
                             mma_f16_pair(d, ad, bd, idesc, accum);
                         } else {
@@ -398,7 +402,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int half = ew >> 2;
         int acc = 0;
         uint32_t acc_phase = 0;
-        uint8_t* stage_buf = epi + ew * C::EBUF * 4096;
         int t, sp, kb_lo, kb_hi;
         for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
             const int i = t / per_batch, r = t - i * per_batch;
@@ -411,15 +414,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const int mrow = m0 + q * 32;
             const int m = mrow + lane;
             const int nvalid = min(C::BN / 32, (g.N - n0 + 31) / 32);
-            int cc[3];
-            batch_coords(g.cb, bidx, cc);
             int64_t row_off = 0;
             if (m < g.M) row_off = decode_off(g.ob, bidx) + decode_off(g.om, m);
             // unit-stride outputs: row offsets are affine in the row index
             const int64_t row_base = decode_off(g.ob, bidx);
             const int64_t mst = g.om.stride[0];
-            // Sum the accumulator slots (fp32) and write one 32x32 chunk held as
-            // lane = row, v[j] = column nc + j.
+            // Strided outputs: sum the accumulator slots (fp32) and write one
+            // 32x32 chunk held as lane = row, v[j] = column nc + j, each element
+            // to its decoded offset.
             auto emit = [&](uint32_t (&v)[32], int c) {
                 const int nc = n0 + c * 32;
                 if constexpr (C::F32) {
@@ -433,45 +435,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                             v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
                     }
                 }
-                if (g.out_tma) {
-                    // Transpose the chunk through a 128B-swizzled staging buffer;
-                    // each store instruction then writes four 128-byte row pieces.
-                    // Global stores need no completion wait, so the buffer is free
-                    // again once read back.
-                    uint8_t* row = stage_buf + lane * 128;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        uint4 w = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                        *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) << 4)) = w;
-                    }
-                    __syncwarp();
-                    const int jj = lane & 7;
-                    const int n = nc + jj * 4;
-                    uint4 w[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) {
-                        const int rr = k * 4 + (lane >> 3);
-                        w[k] = *reinterpret_cast<const uint4*>(stage_buf + rr * 128 + ((jj ^ (rr & 7)) << 4));
-                    }
-                    __syncwarp();
-                    {
-#pragma unroll
-                        for (int k = 0; k < 8; ++k) {
-                            const int r = mrow + k * 4 + (lane >> 3);
-                            if (r < g.M) {
-                                float* dst = g.out + row_base + (int64_t)r * mst + n;
-                                if (n + 4 <= g.N) {
-                                    *reinterpret_cast<uint4*>(dst) = w[k];
-                                } else {
-                                    const uint32_t e4[4] = {w[k].x, w[k].y, w[k].z, w[k].w};
-#pragma unroll
-                                    for (int e = 0; e < 4; ++e)
-                                        if (n + e < g.N) dst[e] = __uint_as_float(e4[e]);
-                                }
-                            }
-                        }
-                    }
-                } else if (m < g.M) {
+                if (m < g.M) {
                     float* o = g.out + row_off;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
@@ -480,17 +444,68 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     }
                 }
             };
+            const int nv = g.phase >= 3 ? nvalid : 0;  // phase gate: no TMEM reads or stores
+            if (g.out_rows) {
+                // Unit-stride rows: each 16-lane half of the warp's quadrant is
+                // read in the 16x256b layout, where four threads hold 8 consecutive
+                // columns (one 32-byte sector) of one row, so every 8-byte store
+                // instruction writes 8 full sectors straight from registers. (A
+                // 32x32b read transposed through swizzled shared memory into 16-byte
+                // stores covering four 128-byte row pieces was measured first: the
+                // staging traffic competed with the operand pipeline for the
+                // shared-memory port and output-bound shapes ran 5-10% slower.)
+                for (int c = half; c < nv; c += NH) {
+                    const int nc = n0 + c * 32;
+                    uint32_t r[2][16];
+                    __syncwarp();
+                    tmem_ld16x256_x4(tbase + c * 32, r[0]);
+                    tmem_ld16x256_x4(tbase + (16u << 16) + c * 32, r[1]);
+                    tmem_ld_wait();
+                    if constexpr (C::F32) {
+                        for (int sl = 1; sl < nslots; ++sl) {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                uint32_t w[16];
+                                __syncwarp();
+                                tmem_ld16x256_x4(tbase + ((uint32_t)(16 * h) << 16) + (uint32_t)(sl * C::BN) + c * 32, w);
+                                tmem_ld_wait();
+#pragma unroll
+                                for (int j = 0; j < 16; ++j)
+                                    r[h][j] = __float_as_uint(__uint_as_float(r[h][j]) + __uint_as_float(w[j]));
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                        for (int rr = 0; rr < 2; ++rr) {
+                            const int row = mrow + 16 * h + 8 * rr + (lane >> 2);
+                            if (row >= g.M) continue;
+                            float* dst = g.out + row_base + (int64_t)row * mst;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int n = nc + 8 * j + 2 * (lane & 3);
+                                const uint32_t x = r[h][4 * j + 2 * rr], y = r[h][4 * j + 2 * rr + 1];
+                                if (n + 2 <= g.N) {
+                                    *reinterpret_cast<uint2*>(dst + n) = make_uint2(x, y);
+                                } else if (n < g.N) {
+                                    dst[n] = __uint_as_float(x);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
             // Two register buffers: the TMEM load of the next chunk is in flight
             // while the current one is written out.
             uint32_t va[32], vb[32];
-            const int nv = g.phase >= 3 ? nvalid : 0;  // phase gate: no TMEM reads or stores
-            if (half < nv) {
+            if (half < nv && !g.out_rows) {
                 __syncwarp();
                 tmem_ld32(tbase + half * 32, va);
                 tmem_ld_wait();
             }
 #pragma unroll 1
-            for (int c = half; c < nv; c += 2 * NH) {
+            for (int c = half; c < (g.out_rows ? 0 : nv); c += 2 * NH) {
                 const int c1 = c + NH, c2 = c + 2 * NH;
                 __syncwarp();
                 if (c1 < nv) tmem_ld32(tbase + c1 * 32, vb);
@@ -869,6 +884,12 @@ int streamk_mode() {
 
 int pairs_enabled() {
     const char* e = getenv("PE_GEMM_PAIRS");
+    return (e && e[0] == '0') ? 0 : 1;
+}
+
+// fp32 3xTF32 on CTA pairs (PE_GEMM_FP32_PAIRS=0 disables)
+int fp32_pairs_enabled() {
+    const char* e = getenv("PE_GEMM_FP32_PAIRS");
     return (e && e[0] == '0') ? 0 : 1;
 }
 
@@ -1826,7 +1847,13 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
         target = (float*)((uint8_t*)ws + L.p_off);
     }
     g.out = target;
-    g.out_tma = encode_output(&g.tmc, target, *ov, &g.cb) ? 1 : 0;
+    {
+        // the layout check of a tensor map over the output: unit-stride rows with
+        // 16-byte aligned strides, at most three batch axes
+        CUtensorMap tm_check;
+        MapBatch mb_check;
+        g.out_rows = encode_output(&tm_check, target, *ov, &mb_check) ? 1 : 0;
+    }
     g.ob = make_decode(ov->b, ov->nb);
     g.om = make_decode(ov->m, ov->nm);
     g.on = make_decode(ov->n, ov->nn);
@@ -1867,7 +1894,18 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
         // both small halves precomputed: the split warps have nothing to do, so
         // spend the threads on epilogue warps instead (output-bound shapes)
         const int64_t tiles256 = pl->I * ((pl->L0 + 127) / 128) * ((pl->L1 + 255) / 256);
-        if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256 >= num_sms() &&
+        const int64_t tiles256x2 = pl->I * ((pl->L0 + 255) / 256) * ((pl->L1 + 255) / 256);
+        if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256x2 >= num_sms() / 2 &&
+            L.sk_q == 0 && L.ksplit <= 1 && wide_fp32_enabled() && pairs_enabled() && fp32_pairs_enabled()) {
+            // CTA pairs on 256x256 tiles: each SM lands its 128 rows of A and half
+            // of B (raw and small halves), so per-SM operand traffic falls by a
+            // quarter on this shared-memory-bound path
+            OperandView vbs = vb;
+            vbs.base = (uint8_t*)ws + L.bs_off;
+            if (!encode_operand(&g.tmb, vb, true, 128) || !encode_operand(&g.tmbs, vbs, true, 128))
+                return set_last_error(PE_ERR_UNSUPPORTED);
+            gemm_step(Cfg<256, true, 8, true, 0>{}, g);
+        } else if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256 >= num_sms() &&
             wide_fp32_enabled()) {
             // wide tiles halve the tf32 MMA count per output column block
             OperandView vbs = vb;

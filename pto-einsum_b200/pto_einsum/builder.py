@@ -318,7 +318,11 @@ class EinsumBuilder:
             cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", "-I", self.include_dir, *extra,
                    self.cpp_filename, "-o", tmp, "-L", LIB_DIR, "-lpto_einsum_b200",
                    f"-Wl,-rpath,{LIB_DIR}"]
-        res = subprocess.run(cmd, capture_output=True, text=True)
+        try:
+            res = subprocess.run(cmd, capture_output=True, text=True)
+        except OSError as e:
+            raise RuntimeError(f"Compilation failed: cannot run the compiler {cxx!r} ({e}); set CXX to a "
+                               "working C++17 compiler") from e
         if res.returncode != 0:
             raise RuntimeError(f"Compilation failed:\n{res.stderr}")
         os.replace(tmp, self.so_filename)  # atomic: concurrent builders never see a partial .so
@@ -379,7 +383,9 @@ class EinsumBuilder:
         if ws is None:
             with torch.cuda.device(dev):
                 ws = self.lib.run_einsum_setup(ctypes.c_void_p(stream_ptr))
-            self._check("run_einsum_setup")
+            if self.lib.run_einsum_last_error():
+                self.lib.run_einsum_teardown(ctypes.c_void_p(ws))
+                self._check("run_einsum_setup")
             self._workspace[dev.index] = ws
         return ws
 
@@ -389,7 +395,14 @@ class EinsumBuilder:
             return self._build_composite()
         self.generate_code()
         self.compile()
-        self.load_library()
+        try:
+            self.load_library()
+        except OSError:
+            # a damaged cache entry (truncated or overwritten .so): rebuild it once;
+            # a second failure is raised
+            os.remove(self.so_filename)
+            self.compile()
+            self.load_library()
         r = self.recipe
         self._splitk = False if (r['elementwise'] or r['broadcast']) else self._splitk_eligible()
         out_shape = tuple(r['out_shape'])
@@ -504,7 +517,7 @@ class EinsumBuilder:
         self._free_workspaces()
         self.lib = None
         if self.target_dir and os.path.exists(self.target_dir):
-            shutil.rmtree(self.target_dir)
+            shutil.rmtree(self.target_dir, ignore_errors=True)  # another process may share the cache
 
 
 def einsum(equation: str, *operands, device="cuda", extended: bool = False):

@@ -64,13 +64,30 @@ def sharded_einsum(equation: str, a_local: torch.Tensor, b_local: torch.Tensor, 
     if not gather:
         return out
     world = dist.get_world_size(group)
+    rest = tuple(out.shape[1:])
     shard = -(-full_size // world)
-    pad = torch.zeros((shard,) + tuple(out.shape[1:]), dtype=out.dtype, device=out.device)
+    if full_size % world == 0:
+        # equal shards: gather straight into the result, no padding or copies
+        full = torch.empty((full_size,) + rest, dtype=out.dtype, device=out.device)
+        _all_gather_into(full, out.contiguous(), group)
+        return full
+    # unequal shards: gather padded shards, then drop each rank's padding
+    pad = torch.zeros((shard,) + rest, dtype=out.dtype, device=out.device)
     pad[: out.shape[0]] = out
-    parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad, group=group)
+    buf = torch.empty((world * shard,) + rest, dtype=out.dtype, device=out.device)
+    _all_gather_into(buf, pad, group)
     pieces = []
     for r in range(world):
         lo, hi = shard_bounds(full_size, world, r)
-        pieces.append(parts[r][: hi - lo])
+        pieces.append(buf[r * shard: r * shard + (hi - lo)])
     return torch.cat(pieces, dim=0)
+
+
+def _all_gather_into(dst: torch.Tensor, src: torch.Tensor, group) -> None:
+    """dst = concatenation of every rank's src along dim 0 (one collective)."""
+    import torch.distributed as dist
+    try:
+        dist.all_gather_into_tensor(dst, src, group=group)
+    except (RuntimeError, NotImplementedError):
+        # backends without the fused form (older gloo): gather into views of dst
+        dist.all_gather(list(dst.chunk(dist.get_world_size(group), dim=0)), src, group=group)

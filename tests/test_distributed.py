@@ -59,6 +59,7 @@ def _worker(rank, world, port, eq, s0, s1, q):
 
 
 @pytest.mark.parametrize("eq,s0,s1", [("bij,bjk->bik", (5, 8, 16), (5, 16, 8)),
+                                      ("bij,bjk->bik", (4, 8, 16), (4, 16, 8)),
                                       ("tn,sn->ts", (9, 16), (12, 16)),
                                       ("hqk,h->hqk", (3, 4, 4), (3,))])
 def test_gloo_two_ranks(eq, s0, s1):

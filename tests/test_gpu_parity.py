@@ -403,3 +403,23 @@ def test_fp32_wide_tiles(eq, s0, s1, monkeypatch):
     narrow = einsum(eq, a.cuda(), b.cuda())
     check_close(narrow, ref, torch.float32)
     assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("eq,s0,s1", [("tn, sn -> ts", (4096, 128), (4096, 128)),
+                                      ("tn, sn -> ts", (4000, 96), (3000, 96)),
+                                      ("bik, bjk -> bij", (8, 1024, 64), (8, 1000, 64))])
+def test_fp32_cta_pairs_match_single_cta_and_oracle(eq, s0, s1, monkeypatch):
+    """3xTF32 on CTA pairs (256x256 tiles, both tf32 small halves precomputed)
+    against the single-CTA wide kernel (PE_GEMM_FP32_PAIRS=0) and the oracle,
+    with ragged row and column tiles."""
+    a, b = seeded(s0, torch.float32, 3, "randn"), seeded(s1, torch.float32, 4, "randn")
+    ref = oracle.einsum_cpu(eq, a, b)
+    outs = []
+    for flag in ("1", "0"):
+        monkeypatch.setenv("PE_GEMM_FP32_PAIRS", flag)
+        bld = EinsumBuilder(eq, [s0, s1], torch.float32)
+        out = bld.build()(a.cuda(), b.cuda())
+        check_close(out, ref, torch.float32)
+        outs.append(out)
+        bld.cleanup()
+    assert _core.device_error(torch.cuda.current_stream().cuda_stream) == 0
