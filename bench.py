@@ -784,6 +784,17 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
                          "how": "about 1 s of back-to-back steps after the timed region; clocks from its second half"},
            "gpu_launches": launches, "clocks": clk}
 
+    if name == "cfg2" and shard:
+        # the same contraction through cuBLAS (torch.bmm, fp16 in, fp32 out) on the
+        # same inputs and stream: a library reference point, not a baseline arm
+        try:
+            bmm = lambda: torch.bmm(a, b, out_dtype=torch.float32)  # noqa: E731
+            t_lib = _max_over_ranks(_time(bmm, steps, 3), dist, device)
+            res["library_reference"] = {
+                "what": "torch.bmm(a, b, out_dtype=torch.float32) (cuBLAS), same inputs, CUDA events",
+                "value": job_units / (t_lib * 1e-3) / scale, "unit": unit, "ms_per_step": t_lib}
+        except (TypeError, RuntimeError) as e:
+            res["library_reference"] = {"unavailable": str(e)[:120]}
     if parity and rank == 0:
         out = run(a, b)
         chk = fullsize.check(name, a.cpu(), b.cpu(), out.cpu(), threads=min(os.cpu_count() or 1, 32),
@@ -1016,7 +1027,7 @@ def main():
                                        "(pto_einsum.distributed.shard_operands), no collective on the data path"),
             "roofline": head["roofline"], "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"],
             "parity": head.get("parity"), "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
-            "sustained": head["sustained"],
+            "sustained": head["sustained"], "library_reference": head.get("library_reference"),
         }
         line.update(extra)
         if cmap:

@@ -11,10 +11,11 @@
  * the reference CPU path. The loop structure is this library's own:
  *  - operands are gathered once into the canonical [I, L0, C] / [I, C, L1]
  *    layouts (the reference's Phase A transposes) with 64-bit indices;
- *  - the product runs over blocks of output columns with the accumulator row
- *    kept in cache and the c loop outermost inside the block, so the inner
- *    loop is a unit-stride vector update acc[j] += a * b[c][j] (per element
- *    still the reference's order);
+ *  - the product runs over groups of four output rows and blocks of 256 output
+ *    columns with the four accumulator rows kept in cache and the c loop
+ *    outermost inside the block, so the inner loop is a unit-stride vector
+ *    update acc_r[j] += a_r * b[c][j] sharing each load of b between the four
+ *    rows (per element still the reference's order);
  *  - rows of output are shared among host threads (std::thread); each element
  *    is computed by exactly one thread, so the thread count never changes a
  *    bit;
@@ -101,24 +102,50 @@ inline int einsum(const T* data0, const T* data1, float* res) {
     }
     for_each_perm<P0>([&](int64_t d, int64_t s) { a[(size_t)d] = static_cast<float>(data0[s]); });
     for_each_perm<P1>([&](int64_t d, int64_t s) { b[(size_t)d] = static_cast<float>(data1[s]); });
-    constexpr int64_t JB = 512;  // output columns per block (2 KB accumulator row)
+    constexpr int64_t JB = 256;  // output columns per block (1 KB accumulator row)
+    constexpr int64_t RB = 4;    // output rows sharing each loaded row of B
     const float* A = a.data();
     const float* B = b.data();
     float* O = o.data();
-    parallel_rows(I * L0, L1 * C, [&](int64_t r0, int64_t r1) {
-        for (int64_t r = r0; r < r1; ++r) {
-            const int64_t i = r / L0;
-            const float* arow = A + r * C;
+    // work items: (batch, group of RB rows); rows of a group share their B loads
+    const int64_t groups = (L0 + RB - 1) / RB;
+    parallel_rows(I * groups, RB * L1 * C, [&](int64_t g0, int64_t g1) {
+        for (int64_t g = g0; g < g1; ++g) {
+            const int64_t i = g / groups;
+            const int64_t l0 = (g - i * groups) * RB;
+            const int64_t nr = std::min(RB, L0 - l0);
             const float* bmat = B + i * C * L1;
-            float* orow = O + r * L1;
             for (int64_t j0 = 0; j0 < L1; j0 += JB) {
                 const int64_t nj = std::min(JB, L1 - j0);
-                float* acc = orow + j0;
-                for (int64_t j = 0; j < nj; ++j) acc[j] = 0.0f;
-                for (int64_t c = 0; c < C; ++c) {
-                    const float av = arow[c];
-                    const float* brow = bmat + c * L1 + j0;
-                    for (int64_t j = 0; j < nj; ++j) acc[j] = acc[j] + av * brow[j];
+                if (nr == RB) {
+                    float* __restrict o0 = O + (i * L0 + l0) * L1 + j0;
+                    float* __restrict o1 = o0 + L1;
+                    float* __restrict o2 = o1 + L1;
+                    float* __restrict o3 = o2 + L1;
+                    const float* a0p = A + (i * L0 + l0) * C;
+                    for (int64_t j = 0; j < nj; ++j) o0[j] = o1[j] = o2[j] = o3[j] = 0.0f;
+                    for (int64_t c = 0; c < C; ++c) {
+                        const float* __restrict brow = bmat + c * L1 + j0;
+                        const float a0 = a0p[c], a1 = a0p[C + c], a2 = a0p[2 * C + c], a3 = a0p[3 * C + c];
+                        for (int64_t j = 0; j < nj; ++j) {
+                            const float bv = brow[j];
+                            o0[j] = o0[j] + a0 * bv;
+                            o1[j] = o1[j] + a1 * bv;
+                            o2[j] = o2[j] + a2 * bv;
+                            o3[j] = o3[j] + a3 * bv;
+                        }
+                    }
+                } else {
+                    for (int64_t r = 0; r < nr; ++r) {
+                        float* __restrict o0 = O + (i * L0 + l0 + r) * L1 + j0;
+                        const float* arow = A + (i * L0 + l0 + r) * C;
+                        for (int64_t j = 0; j < nj; ++j) o0[j] = 0.0f;
+                        for (int64_t c = 0; c < C; ++c) {
+                            const float* __restrict brow = bmat + c * L1 + j0;
+                            const float a0 = arow[c];
+                            for (int64_t j = 0; j < nj; ++j) o0[j] = o0[j] + a0 * brow[j];
+                        }
+                    }
                 }
             }
         }

@@ -454,13 +454,12 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 // stores covering four 128-byte row pieces was measured first: the
                 // staging traffic competed with the operand pipeline for the
                 // shared-memory port and output-bound shapes ran 5-10% slower.)
-                for (int c = half; c < nv; c += NH) {
-                    const int nc = n0 + c * 32;
-                    uint32_t r[2][16];
-                    __syncwarp();
+                auto load_chunk = [&](uint32_t (&r)[2][16], int c) {
                     tmem_ld16x256_x4(tbase + c * 32, r[0]);
                     tmem_ld16x256_x4(tbase + (16u << 16) + c * 32, r[1]);
-                    tmem_ld_wait();
+                };
+                auto store_chunk = [&](uint32_t (&r)[2][16], int c) {
+                    const int nc = n0 + c * 32;
                     if constexpr (C::F32) {
                         for (int sl = 1; sl < nslots; ++sl) {
 #pragma unroll
@@ -494,6 +493,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                             }
                         }
                     }
+                };
+                // One register buffer: measured against two (the next chunk's TMEM
+                // reads in flight while the current chunk is stored), which spilled
+                // and ran 10-15% slower on the output-bound configs.
+                uint32_t ra[2][16];
+                for (int c = half; c < nv; c += NH) {
+                    __syncwarp();
+                    load_chunk(ra, c);
+                    tmem_ld_wait();
+                    store_chunk(ra, c);
                 }
             }
             // Two register buffers: the TMEM load of the next chunk is in flight
