@@ -584,6 +584,73 @@ def run_base_suite(args):
             print(json.dumps(row), flush=True)
 
 
+def run_kda_suite(args):
+    """KDA stage backends (the reference's benchmarks/complex/kda/bench_kda_4way.py
+    workloads: N_seq x L_seg in {1,2} x {512,1024}, H=32 value heads, Hk=16 key heads,
+    head dim 128, chunk 128, fp32, per-dimension gate in (-0.05, 0]): per stage median
+    device time with a 256 MB L2 flush before each sample, torch.einsum backend vs
+    this library's kernels on the same glue, the whole forward eager and as one CUDA
+    graph, and the relative Frobenius error against the same pipeline in float64."""
+    from pto_einsum.kda import KDAChunked, KDAGraph, random_kda_inputs
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(256 << 20, dtype=torch.int8, device=dev)
+    iters = max(args.steps // 10, 10)
+
+    def med(fn, warmup=3):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2]
+
+    def rel(a, b):
+        a, b = a.double(), b.double()
+        return ((a - b).norm() / b.norm()).item()
+
+    H, Hk, D, C = 32, 16, 128, 128
+    for n_seq, l_seg in [(1, 512), (2, 512), (1, 1024), (2, 1024)]:
+        T = n_seq * l_seg
+        cu = list(range(0, T + 1, l_seg))
+        q, k, v, g, beta = random_kda_inputs(T, H, Hk, D, seed=T + n_seq, device=dev)
+        scale = D ** -0.5
+        row = {"suite": "kda", "N_seq": n_seq, "L_seg": l_seg, "T": T, "H": H, "Hk": Hk, "D": D, "chunk": C,
+               "dtype": "float32"}
+        ref = KDAChunked("torch", chunk=C, dtype=torch.float64)(
+            *(x.double() for x in (q, k, v, g, beta)), scale=scale, cu_seqlens=cu)
+        for name in ("torch", "pto"):
+            m = KDAChunked(name, chunk=C)
+            f = lambda x: m.fold(x, cu)  # noqa: E731
+            qf, kf, vf, gf, bf = f(q), f(k), f(v), f(g), f(beta)
+            gcum = m.cumsum(gf)
+            A = m.kkt(kf, bf, gcum)
+            Ainv = m.solve_tril(A)
+            w, u = m.wy_fast(kf, vf, bf, Ainv, gcum)
+            h, vn, _ = m.chunk_h(kf, w, u, gcum)
+            stages = {
+                "kkt": lambda: m.kkt(kf, bf, gcum),
+                "wy_fast": lambda: m.wy_fast(kf, vf, bf, Ainv, gcum),
+                "chunk_h": lambda: m.chunk_h(kf, w, u, gcum),
+                "chunk_o": lambda: m.chunk_o(qf, kf, vn, h, gcum),
+            }
+            row[f"{name}_stage_ms"] = {st: round(med(fn), 4) for st, fn in stages.items()}
+            row[f"{name}_forward_ms"] = round(med(lambda: m(q, k, v, g, beta, scale=scale, cu_seqlens=cu)), 4)
+            graph = KDAGraph(m, q, k, v, g, beta, scale=scale, cu_seqlens=cu)
+            row[f"{name}_forward_graph_ms"] = round(med(lambda: graph(q, k, v, g, beta)), 4)
+            row[f"{name}_rel_err_vs_fp64"] = rel(m(q, k, v, g, beta, scale=scale, cu_seqlens=cu), ref)
+            del graph
+            if name == "pto":
+                m.cleanup()
+        print(json.dumps(row), flush=True)
+
+
 def run_gdn_suite(args):
     """GDN stage backends (the reference's benchmarks/complex/gdn/bench_gdn_4way.py
     workloads: N_seq x L_seg in {1,2} x {512,1024}, H=32 value heads, Hg=16 key heads,
@@ -672,7 +739,7 @@ def _barrier(dist, device):
 
 
 def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True, cpu=False, parity=True,
-            e2e=True):
+            e2e=True, sustained_ms=None):
     """Time config `name` through the public EinsumBuilder runner.
 
     shard=True: the config's leading output axis is split over the ranks with
@@ -682,6 +749,8 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     from seeded generators (the shards concatenate to the one-device inputs)."""
     from pto_einsum import EinsumBuilder, _core
     from pto_einsum.distributed import shard_operands
+    t_start = time.time()
+    sustained_ms = args.sustained_ms if sustained_ms is None else sustained_ms
     eq, _, _, dt = CFG[name]
     dtype = getattr(torch, dt)
     full = work(name)
@@ -732,7 +801,7 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     # Sustained: about one second of back-to-back steps, where the 1 kW power
     # cap settles the clocks; reported beside the K-step figure.
     per_step_ms = max(elapsed_ms / steps, 1e-3)
-    n_sus = min(max(steps, int(args.sustained_ms / per_step_ms)), 20000) if args.sustained_ms > 0 else steps
+    n_sus = min(max(steps, int(sustained_ms / per_step_ms)), 20000) if sustained_ms > 0 else steps
     _barrier(dist, device)
     s0e, s1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_s0 = time.time()
@@ -817,6 +886,7 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     builder.cleanup()
     del a, b
     torch.cuda.empty_cache()
+    res["wall_s"] = round(time.time() - t_start, 2)
     return res
 
 
@@ -948,7 +1018,7 @@ def main():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=16,
                     help="pipelined end-to-end steps (fill and drain cost about one step)")
-    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "base", "thin", "host", "phases"],
+    ap.add_argument("--suite", default=None, choices=["callers", "permute", "gdn", "kda", "base", "thin", "host", "phases"],
                     help="instead of the one-line benchmark: one JSON line per op of that suite")
     ap.add_argument("--sustained-ms", type=float, default=1000.0,
                     help="length of the sustained back-to-back run after the timed region (0: K steps only)")
@@ -971,12 +1041,14 @@ def main():
         run_reference_arm(args, rank, world)
         return
     suites = {"callers": run_callers_suite, "permute": run_permute_suite, "gdn": run_gdn_suite,
+              "kda": run_kda_suite,
               "base": run_base_suite, "thin": run_thin_suite, "host": run_host_suite,
               "phases": run_phases_suite}
     if args.suite:
         suites[args.suite](args)
         return
 
+    t_main = time.time()
     dist = None
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
@@ -1008,9 +1080,14 @@ def main():
         others = [n for n in CFG if n != name and n != "cfg1"] if args.configs == "all" else \
             [n for n in args.configs.split(",") if n and n != name]
     cmap = {}
+    # At N > 1 the other configs are timed without their end-to-end, parity and
+    # sustained extras (those are per-GPU properties measured at N = 1), so the
+    # scaling runs hold the GPUs briefly.
+    light = world > 1
     for n in others:
         cmap[n] = measure(n, args, rank, world, dist, device, clocks, steps=args.steps, cpu=want_cpu,
-                          parity=not args.no_parity)
+                          parity=not args.no_parity and not light, e2e=not light,
+                          sustained_ms=0 if light else min(args.sustained_ms, 500.0))
     if world == 1 and args.configs != "none":
         cmap["cfg1"] = measure_cpu_path("cfg1", args)
     clocks.stop()
@@ -1030,6 +1107,7 @@ def main():
             "sustained": head["sustained"], "library_reference": head.get("library_reference"),
         }
         line.update(extra)
+        line["bench_wall_s"] = round(time.time() - t_main, 1)
         if cmap:
             line["configs"] = {n: {k: v for k, v in r.items() if k not in ("metric",)} for n, r in cmap.items()}
         print(json.dumps(line))
