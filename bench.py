@@ -780,22 +780,23 @@ def measure(name, args, rank, world, dist, device, clocks, *, steps, shard=True,
     torch.cuda.synchronize(device)
     _barrier(dist, device)
     launches0 = _core.launch_count()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    # Only the two events that bracket the region: an event recorded between two
+    # steps would sit between their launches and stop the next launch's prologue
+    # from overlapping the previous one's tail (programmatic dependent launch),
+    # which a caller running steps back to back gets.
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_win0 = time.time()
     start.record(stream)
     for k in range(steps):
         j = k % nsets
-        evs[k][0].record(stream)
         outs[j] = run(*sets[j])
-        evs[k][1].record(stream)
     stop.record(stream)
     torch.cuda.synchronize(device)
     t_win1 = time.time()
     launches = _core.launch_count() - launches0
     _barrier(dist, device)
     elapsed_ms = _max_over_ranks(start.elapsed_time(stop), dist, device)
-    per_launch_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    per_launch_ms = start.elapsed_time(stop) / steps  # this rank's mean step (one runner call)
     clk = clocks.summary(t_win0, t_win1)
 
     # Sustained: about one second of back-to-back steps, where the 1 kW power

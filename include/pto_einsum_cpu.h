@@ -58,12 +58,52 @@ inline void for_each_perm(F f) {
     }
 }
 
+/* Block updates of the product, compiled for AVX-512, AVX2 and baseline x86-64
+ * and picked at load time (GNU ifunc). Vector lanes run over output columns
+ * only, so each element still adds its products in c order, one rounding per
+ * product and per sum (-ffp-contract=off keeps multiply and add separate). */
+#if defined(__x86_64__) && defined(__GNUC__) && !defined(__clang__)
+#define PE_CPU_CLONES __attribute__((target_clones("avx512f", "avx2", "default")))
+#else
+#define PE_CPU_CLONES
+#endif
+
+/* Four output rows o0..o3 (columns [0, nj)) = sum over c of a_r[c] * brow_c. */
+PE_CPU_CLONES __attribute__((noinline)) static void block4(const float* a0p, int64_t C, const float* bcol,
+                                                           int64_t L1, int64_t nj, float* __restrict o0,
+                                                           float* __restrict o1, float* __restrict o2,
+                                                           float* __restrict o3) {
+    for (int64_t j = 0; j < nj; ++j) o0[j] = o1[j] = o2[j] = o3[j] = 0.0f;
+    for (int64_t c = 0; c < C; ++c) {
+        const float* __restrict brow = bcol + c * L1;
+        const float a0 = a0p[c], a1 = a0p[C + c], a2 = a0p[2 * C + c], a3 = a0p[3 * C + c];
+        for (int64_t j = 0; j < nj; ++j) {
+            const float bv = brow[j];
+            o0[j] = o0[j] + a0 * bv;
+            o1[j] = o1[j] + a1 * bv;
+            o2[j] = o2[j] + a2 * bv;
+            o3[j] = o3[j] + a3 * bv;
+        }
+    }
+}
+
+/* One output row. */
+PE_CPU_CLONES __attribute__((noinline)) static void block1(const float* arow, int64_t C, const float* bcol,
+                                                           int64_t L1, int64_t nj, float* __restrict o0) {
+    for (int64_t j = 0; j < nj; ++j) o0[j] = 0.0f;
+    for (int64_t c = 0; c < C; ++c) {
+        const float* __restrict brow = bcol + c * L1;
+        const float a0 = arow[c];
+        for (int64_t j = 0; j < nj; ++j) o0[j] = o0[j] + a0 * brow[j];
+    }
+}
+
 template <class F>
 inline void parallel_rows(int64_t rows, int64_t work_per_row, F f) {
     unsigned hw = std::thread::hardware_concurrency();
     int64_t nt = hw ? hw : 1;
-    // about 4M multiply-adds per thread at least, so small problems stay serial
-    nt = std::min<int64_t>(nt, std::max<int64_t>(1, rows * work_per_row / (int64_t)(4 << 20)));
+    // about 1M multiply-adds per thread at least, so small problems stay serial
+    nt = std::min<int64_t>(nt, std::max<int64_t>(1, rows * work_per_row / (int64_t)(1 << 20)));
     nt = std::min<int64_t>(nt, rows);
     if (nt <= 1) {
         f(0, rows);
@@ -118,34 +158,11 @@ inline int einsum(const T* data0, const T* data1, float* res) {
             for (int64_t j0 = 0; j0 < L1; j0 += JB) {
                 const int64_t nj = std::min(JB, L1 - j0);
                 if (nr == RB) {
-                    float* __restrict o0 = O + (i * L0 + l0) * L1 + j0;
-                    float* __restrict o1 = o0 + L1;
-                    float* __restrict o2 = o1 + L1;
-                    float* __restrict o3 = o2 + L1;
-                    const float* a0p = A + (i * L0 + l0) * C;
-                    for (int64_t j = 0; j < nj; ++j) o0[j] = o1[j] = o2[j] = o3[j] = 0.0f;
-                    for (int64_t c = 0; c < C; ++c) {
-                        const float* __restrict brow = bmat + c * L1 + j0;
-                        const float a0 = a0p[c], a1 = a0p[C + c], a2 = a0p[2 * C + c], a3 = a0p[3 * C + c];
-                        for (int64_t j = 0; j < nj; ++j) {
-                            const float bv = brow[j];
-                            o0[j] = o0[j] + a0 * bv;
-                            o1[j] = o1[j] + a1 * bv;
-                            o2[j] = o2[j] + a2 * bv;
-                            o3[j] = o3[j] + a3 * bv;
-                        }
-                    }
+                    float* o0 = O + (i * L0 + l0) * L1 + j0;
+                    block4(A + (i * L0 + l0) * C, C, bmat + j0, L1, nj, o0, o0 + L1, o0 + 2 * L1, o0 + 3 * L1);
                 } else {
-                    for (int64_t r = 0; r < nr; ++r) {
-                        float* __restrict o0 = O + (i * L0 + l0 + r) * L1 + j0;
-                        const float* arow = A + (i * L0 + l0 + r) * C;
-                        for (int64_t j = 0; j < nj; ++j) o0[j] = 0.0f;
-                        for (int64_t c = 0; c < C; ++c) {
-                            const float* __restrict brow = bmat + c * L1 + j0;
-                            const float a0 = arow[c];
-                            for (int64_t j = 0; j < nj; ++j) o0[j] = o0[j] + a0 * brow[j];
-                        }
-                    }
+                    for (int64_t r = 0; r < nr; ++r)
+                        block1(A + (i * L0 + l0 + r) * C, C, bmat + j0, L1, nj, O + (i * L0 + l0 + r) * L1 + j0);
                 }
             }
         }

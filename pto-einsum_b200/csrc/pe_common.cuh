@@ -47,6 +47,18 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
 
+// Programmatic dependent launch: wait until the grids this launch depends on
+// have completed and their memory is visible; allow dependents to launch.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// 32-byte store (sm_100 256-bit vector store); p must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(float* p, const uint32_t (&v)[4][2]) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0][0]), "r"(v[0][1]),
+                 "r"(v[1][0]), "r"(v[1][1]), "r"(v[2][0]), "r"(v[2][1]), "r"(v[3][0]), "r"(v[3][1])
+                 : "memory");
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

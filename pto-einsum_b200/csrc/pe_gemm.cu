@@ -65,6 +65,7 @@ struct GemmArgs {
     int a_mn, b_mn;
     MapBatch ab, bb;
     int out_rows;    // output rows unit-stride with 16-byte aligned strides (full-sector stores)
+    int out_v8;      // and 32-byte aligned rows: full-line 32-byte stores after a quad transpose
     int acc_slots;   // fp32: accumulator slots per tile (1, 2 or 4)
     int ksplit;      // work units per output tile (split-K), >= 1
     int kper;        // k-iterations per unit
@@ -77,7 +78,8 @@ struct GemmArgs {
     Decode ob, om, on;
 };
 
-template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8), bool PAIR_ = false, int SPLITW_ = (F32_ ? 4 : 0)>
+template <int BN_, bool F32_, int EPIW_ = (F32_ ? 4 : 8), bool PAIR_ = false, int SPLITW_ = (F32_ ? 4 : 0),
+          int KB_ = 1>
 struct Cfg {
     // PAIR: a cluster of two CTAs computes one TM = 256-row tile with
     // tcgen05 cta_group::2; each CTA lands 128 rows of A and half of B's N.
@@ -87,11 +89,16 @@ struct Cfg {
     static constexpr int BN = BN_;
     static constexpr bool F32 = F32_;
     static constexpr int ES = F32 ? 4 : 2;
-    static constexpr int BK = 128 / ES;                 // one 128-byte swizzle row
+    // KB 128-byte swizzle rows of the contraction per stage: K-major operands
+    // land as KB boxes side by side (each a [rows][128 B] block), MN-major
+    // operands as one box of BK rows per 128-byte column block. Two rows per
+    // stage halve the barrier handoffs and MMA commits per FLOP.
+    static constexpr int KB = KB_;
+    static constexpr int BK = KB * 128 / ES;
     static constexpr int MNBOX = 128 / ES;              // MN-major box width
-    static constexpr int A_BYTES = BM * 128;
+    static constexpr int A_BYTES = BM * 128 * KB;
     static constexpr int BNL = PAIR ? BN / 2 : BN;     // B columns landed per CTA
-    static constexpr int B_BYTES = BNL * 128;
+    static constexpr int B_BYTES = BNL * 128 * KB;
     static constexpr int TX_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE_BYTES = TX_BYTES * (F32 ? 2 : 1);
     // epilogue warps: 4 (one per TMEM lane quadrant) or more, sharing quadrants
@@ -102,6 +109,7 @@ struct Cfg {
     static constexpr int STAGES = (224 * 1024) / STAGE_BYTES;
     static constexpr int UMMA_K = F32 ? 8 : 16;
     static constexpr int KSUB = BK / UMMA_K;
+    static constexpr int KSUB1 = 128 / ES / UMMA_K;     // MMA k-steps per 128-byte row
     // fp32: each accumulator buffer holds two BN-column sums (big*big and the
     // two cross terms), added with one IEEE fp32 add in the epilogue
     // TMEM holds 4 (fp32) or 2 (fp16) BN-column slots. fp16: two accumulator
@@ -120,6 +128,7 @@ struct Cfg {
     static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
     // fp32 pairs only with both tf32 small halves precomputed (no split warps)
     static_assert(!PAIR || !F32 || SPLITW == 0, "fp32 CTA pairs need precomputed small halves");
+    static_assert(KB == 1 || !F32, "two-row stages are fp16 only");
 };
 
 // Batch coordinates of flat batch index i in one map (fully unrolled so the
@@ -182,6 +191,23 @@ __device__ __forceinline__ bool work_unit(const GemmArgs& g, int unit0, int uste
     return true;
 }
 
+// Diagnostic build (-DPE_STALL_STATS): per-CTA cycle counts of each pipeline
+// role's waits, read back with pe_stall_stats(). Slots: 0 producer waiting for a
+// free stage, 1 MMA thread waiting for landed operands, 2 MMA thread waiting for
+// a drained accumulator, 3 epilogue warp 2 waiting for a finished accumulator,
+// 4 epilogue warp 2 busy (accumulator ready -> handed back), 5 kernel cycles
+// (thread 0), 6 tiles.
+#ifdef PE_STALL_STATS
+__device__ unsigned long long pe_stall[1024 * 8];
+#define PE_STALL_BEGIN() const long long _st0 = clock64()
+#define PE_STALL_END(slot) atomicAdd(&pe_stall[blockIdx.x * 8 + (slot)], (unsigned long long)(clock64() - _st0))
+#define PE_STALL_ADD(slot, v) atomicAdd(&pe_stall[blockIdx.x * 8 + (slot)], (unsigned long long)(v))
+#else
+#define PE_STALL_BEGIN() ((void)0)
+#define PE_STALL_END(slot) ((void)0)
+#define PE_STALL_ADD(slot, v) ((void)0)
+#endif
+
 template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmArgs g) {
     extern __shared__ uint8_t smem_raw[];
@@ -236,6 +262,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const int per_batch = g.mblk * g.nblk;
+    // Programmatic dependent launch: the prologue above (barrier init, TMEM
+    // allocation, descriptor prefetch) overlaps the previous kernel's tail; no
+    // global memory is read or written before the previous grid has finished.
+    // Dependents are released at once: they only become resident as this
+    // grid's CTAs exit, and they wait the same way.
+    grid_dep_wait();
+    grid_dep_launch();
+#ifdef PE_STALL_STATS
+    const long long k_t0 = clock64();
+#endif
 
     if (warp == 0) {
         if (lane == 0) {
@@ -252,7 +288,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                 batch_coords(g.ab, i, ca);
                 batch_coords(g.bb, i, cb);
                 for (int kb = kb_lo; kb < kb_hi; ++kb) {
+                    PE_STALL_BEGIN();
                     if (!mbar_wait(empty(stage), phase ^ 1, abort_flag, 1)) break;
+                    PE_STALL_END(0);
                     uint8_t* sa = smem + stage * C::STAGE_BYTES;
                     uint8_t* sb = sa + C::A_BYTES;
                     const int k0 = kb * C::BK;
@@ -280,7 +318,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     };
                     auto load_a = [&](uint8_t* dst, const CUtensorMap* tm) {
                         if (!g.a_mn) {
-                            load(smem_u32(dst), tm, k0, m0, ca);
+#pragma unroll
+                            for (int u = 0; u < C::KB; ++u)
+                                load(smem_u32(dst + u * C::BM * 128), tm, k0 + u * C::MNBOX, m0, ca);
                         } else {
 #pragma unroll
                             for (int j = 0; j < C::BM / C::MNBOX; ++j)
@@ -289,7 +329,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     };
                     auto load_b = [&](uint8_t* dst, const CUtensorMap* tm) {
                         if (!g.b_mn) {
-                            load(smem_u32(dst), tm, k0, n0, cb);
+#pragma unroll
+                            for (int u = 0; u < C::KB; ++u)
+                                load(smem_u32(dst + u * C::BNL * 128), tm, k0 + u * C::MNBOX, n0, cb);
                         } else {
 #pragma unroll
                             for (int j = 0; j < C::BNL / C::MNBOX; ++j)
@@ -332,15 +374,21 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             uint32_t phase = 0, acc_phase = 0;
             int t, sp, kb_lo, kb_hi;
             for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
-                if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
+                {
+                    PE_STALL_BEGIN();
+                    if (!mbar_wait(tempty(acc), acc_phase ^ 1, abort_flag, 2)) break;
+                    PE_STALL_END(2);
+                }
                 tc_fence_after();
                 const uint32_t dbuf = tmem_base + (uint32_t)(acc * S * C::BN);
                 bool ok = true;
                 for (int kb = kb_lo; kb < kb_hi; ++kb) {
+                    PE_STALL_BEGIN();
                     if (!mbar_wait(C::F32 && !split_done_by_tma ? split(stage) : full(stage), phase, abort_flag, 3)) {
                         ok = false;
                         break;
                     }
+                    PE_STALL_END(1);
                     tc_fence_after();
                     const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
                     const uint32_t sb = sa + C::A_BYTES;
@@ -349,8 +397,13 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
 #pragma unroll
                     for (int ks = 0; ks < C::KSUB; ++ks) {
                         if (g.phase < 2) break;  // phase gate: no MMAs
-                        const uint64_t ad = smem_desc_sw128(sa + ks * a_kstep, a_lbo, a_sbo, a_lay);
-                        const uint64_t bd = smem_desc_sw128(sb + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                        // K-major: k-step ks lies in row block ks / KSUB1 of the stage
+                        const uint32_t a_off = g.a_mn ? ks * a_kstep
+                                                      : (ks / C::KSUB1) * (C::BM * 128) + (ks % C::KSUB1) * a_kstep;
+                        const uint32_t b_off = g.b_mn ? ks * b_kstep
+                                                      : (ks / C::KSUB1) * (C::BNL * 128) + (ks % C::KSUB1) * b_kstep;
+                        const uint64_t ad = smem_desc_sw128(sa + a_off, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = smem_desc_sw128(sb + b_off, b_lbo, b_sbo, b_lay);
                         const uint32_t accum = (kb - kb_lo >= S || ks > 0) ? 1u : 0u;
                         if constexpr (C::F32) {
                             const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, a_sbo, a_lay);
@@ -406,7 +459,17 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         for (int idx = 0; !*abort_flag && work_unit(g, unit0, ustep, idx, t, sp, kb_lo, kb_hi); ++idx) {
             const int i = t / per_batch, r = t - i * per_batch;
             const int m0 = (r / g.nblk) * C::TM + (int)rank * C::BM, n0 = (r % g.nblk) * C::BN;
+#ifdef PE_STALL_STATS
+            const long long e_t0 = clock64();
+#endif
             if (!mbar_wait(tfull(acc), acc_phase, abort_flag, 4)) break;
+#ifdef PE_STALL_STATS
+            const long long e_t1 = clock64();
+            if (ew == 0 && lane == 0) {
+                PE_STALL_ADD(3, e_t1 - e_t0);
+                PE_STALL_ADD(6, 1);
+            }
+#endif
             tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * S * C::BN);
             const int nslots = S < kb_hi - kb_lo ? S : kb_hi - kb_lo;
@@ -474,6 +537,63 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                             }
                         }
                     }
+                    if (g.out_v8) {
+                        // The four lanes of a quad hold one row: lane q has the column
+                        // pairs 8j + 2q (j = 0..3). A two-stage butterfly (xor 1, then
+                        // xor 2) transposes the 4x4 pair matrix so that lane q holds
+                        // columns 8q..8q+7, and one 32-byte store per lane writes the
+                        // row's 128 bytes: eight full lines per warp instruction instead
+                        // of eight 32-byte sectors.
+                        const bool ql = lane & 1, qh = (lane >> 1) & 1;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                            for (int rr = 0; rr < 2; ++rr) {
+                                uint32_t e[4][2], f[2][2][2], o[4][2];
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) {
+                                    e[j][0] = r[h][4 * j + 2 * rr];
+                                    e[j][1] = r[h][4 * j + 2 * rr + 1];
+                                }
+                                // stage 1: keep the pair with j's low bit = ql, swap the other
+#pragma unroll
+                                for (int jh = 0; jh < 2; ++jh) {
+#pragma unroll
+                                    for (int w = 0; w < 2; ++w) {
+                                        const uint32_t send = ql ? e[2 * jh][w] : e[2 * jh + 1][w];
+                                        const uint32_t keep = ql ? e[2 * jh + 1][w] : e[2 * jh][w];
+                                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                                        f[jh][0][w] = ql ? recv : keep;
+                                        f[jh][1][w] = ql ? keep : recv;
+                                    }
+                                }
+                                // stage 2: keep jh = qh, swap the other
+#pragma unroll
+                                for (int rl = 0; rl < 2; ++rl) {
+#pragma unroll
+                                    for (int w = 0; w < 2; ++w) {
+                                        const uint32_t send = qh ? f[0][rl][w] : f[1][rl][w];
+                                        const uint32_t keep = qh ? f[1][rl][w] : f[0][rl][w];
+                                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 2);
+                                        o[rl][w] = qh ? recv : keep;
+                                        o[2 + rl][w] = qh ? keep : recv;
+                                    }
+                                }
+                                const int row = mrow + 16 * h + 8 * rr + (lane >> 2);
+                                if (row >= g.M) continue;
+                                float* dst = g.out + row_base + (int64_t)row * mst;
+                                const int n = nc + 8 * (lane & 3);
+                                if (n + 8 <= g.N) {
+                                    st_global_v8(dst + n, o);
+                                } else {
+#pragma unroll
+                                    for (int j = 0; j < 8; ++j)
+                                        if (n + j < g.N) dst[n + j] = __uint_as_float(o[j >> 1][j & 1]);
+                                }
+                            }
+                        }
+                        return;
+                    }
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -532,6 +652,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             if (lane == 0) {
                 if constexpr (C::PAIR) mbar_arrive_cluster(map_to_rank(tempty(acc), 0));  // leader's barrier
                 else mbar_arrive(tempty(acc));
+#ifdef PE_STALL_STATS
+                if (ew == 0) PE_STALL_ADD(4, clock64() - e_t1);
+#endif
             }
             if (++acc == NBUF) {
                 acc = 0;
@@ -582,6 +705,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     }
 
     __syncthreads();
+#ifdef PE_STALL_STATS
+    if (threadIdx.x == 0) PE_STALL_ADD(5, clock64() - k_t0);
+#endif
     // pairs: the leader's MMAs write the peer's TMEM and both CTAs' barriers
     // receive remote arrivals, so neither CTA leaves before the other is done
     if constexpr (C::PAIR) cluster_sync();
@@ -678,7 +804,7 @@ OperandView view_direct(const void* base, int es, const Axis* batch, int nb, con
 }
 
 // Rank-5 tensor map of an operand view: dims {inner, outer, batch0..2}.
-bool encode_operand(CUtensorMap* tm, const OperandView& v, bool f32, int box_mn_rows) {
+bool encode_operand(CUtensorMap* tm, const OperandView& v, bool f32, int box_mn_rows, int box_k_rows = 0) {
     auto enc = get_encode();
     if (!enc) return false;
     const int es = f32 ? 4 : 2;
@@ -698,7 +824,7 @@ bool encode_operand(CUtensorMap* tm, const OperandView& v, bool f32, int box_mn_
         dims[1] = (cuuint64_t)v.k_size;
         strides[0] = (cuuint64_t)((v.k_size == 1 ? 1 : v.k_stride) * es);
         box[0] = bk;
-        box[1] = bk;
+        box[1] = box_k_rows > 0 ? box_k_rows : bk;
     }
     int64_t ext = 16;  // any valid stride for padded size-1 dims
     for (int j = 0; j < kMaxBatchMap; ++j) {
@@ -782,6 +908,27 @@ bool encode_output(CUtensorMap* tm, float* out, const OutView& o, MapBatch* mb) 
     return true;
 }
 
+// Every output row starts on a 32-byte boundary: base and the row and batch
+// strides (elements) multiples of 8.
+bool rows_aligned32(const float* out, const OutView& o) {
+    if ((uintptr_t)out & 31) return false;
+    for (int j = 0; j < o.nm; ++j)
+        if (o.m[j].size > 1 && (o.m[j].stride & 7)) return false;
+    for (int j = 0; j < o.nb; ++j)
+        if (o.b[j].size > 1 && (o.b[j].stride & 7)) return false;
+    return true;
+}
+
+// Full-line epilogue stores: on by default for single-CTA tiles (output-bound
+// shapes gained 2-6%), off for CTA pairs (3% slower there: the pair mainloop
+// is operand-load bound and the shuffles lengthen the epilogue). PE_EPI_V8=0/1
+// forces either.
+int epi_v8_enabled(bool pair) {
+    const char* e = getenv("PE_EPI_V8");
+    if (e && (e[0] == '0' || e[0] == '1')) return e[0] - '0';
+    return pair ? 0 : 1;
+}
+
 Decode make_decode(const Axis* ax, int n) {
     Decode d{};
     Axis c[PE_MAX_RANK];
@@ -798,6 +945,58 @@ Decode make_decode(const Axis* ax, int n) {
         d.stride[a] = c[a].stride;
     }
     return d;
+}
+
+// Diagnostic: PE_GEMM_GRID_CAP=n runs the persistent grid on at most n SMs
+// (used to tell a per-SM latency limit from a shared-bandwidth limit).
+static int grid_cap() {
+    static int cap = -1;
+    if (cap < 0) {
+        const char* e = getenv("PE_GEMM_GRID_CAP");
+        const int v = e ? atoi(e) : 0;
+        cap = (v > 0 && v < num_sms()) ? v : num_sms();
+    }
+    return cap;
+}
+
+// PE_GEMM_PDL=0 launches without programmatic dependent launch.
+int pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("PE_GEMM_PDL");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on;
+}
+
+// One persistent launch: clusters of `cluster` CTAs (1 = none), programmatic
+// stream serialisation so that the prologue overlaps the previous kernel.
+template <class C>
+int launch_persistent(const GemmArgs& g, int grid, int cluster, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<C>, g);
+    count_launch();
+    return check_cuda(e);
 }
 
 template <class C>
@@ -836,33 +1035,15 @@ int launch_gemm(GemmArgs& g, cudaStream_t s) {
         if (C::PAIR || (g.kiters + g.sk_q - 1) / g.sk_q + 1 > g.ksplit) return set_last_error(PE_ERR_INVALID);
         const int64_t grid = (tiles * g.kiters + g.sk_q - 1) / g.sk_q;
         if (grid > num_sms()) return set_last_error(PE_ERR_INVALID);
-        gemm_kernel<C><<<(int)grid, C::THREADS, C::SMEM, s>>>(g);
-        count_launch();
-        return check_cuda(cudaGetLastError());
+        return launch_persistent<C>(g, (int)grid, 1, s);
     }
     if constexpr (C::PAIR) {
         // one cluster of two CTAs per tile pair, persistent over the SMs
-        const int pairs = (int)std::min<int64_t>(tiles * g.ksplit, num_sms() / 2);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(2 * pairs);
-        cfg.blockDim = dim3(C::THREADS);
-        cfg.dynamicSmemBytes = C::SMEM;
-        cfg.stream = s;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 2;
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<C>, g);
-        count_launch();
-        return check_cuda(e);
+        const int pairs = (int)std::min<int64_t>(tiles * g.ksplit, grid_cap() / 2);
+        return launch_persistent<C>(g, 2 * pairs, 2, s);
     }
-    int grid = std::min<int64_t>(tiles * g.ksplit, num_sms());
-    gemm_kernel<C><<<grid, C::THREADS, C::SMEM, s>>>(g);
-    count_launch();
-    return check_cuda(cudaGetLastError());
+    const int grid = (int)std::min<int64_t>(tiles * g.ksplit, grid_cap());
+    return launch_persistent<C>(g, grid, 1, s);
 }
 
 // fp32 3xTF32: the tensor core reads only the upper 19 bits of each fp32
@@ -900,6 +1081,14 @@ int pairs_enabled() {
 int fp32_pairs_enabled() {
     const char* e = getenv("PE_GEMM_FP32_PAIRS");
     return (e && e[0] == '0') ? 0 : 1;
+}
+
+// fp16 contraction rows per pipeline stage (1 or 2): PE_GEMM_KB overrides the
+// default for CTA pairs and for single CTAs.
+int stage_rows(bool pair) {
+    const char* e = getenv("PE_GEMM_KB");
+    if (e && (e[0] == '1' || e[0] == '2')) return e[0] - '0';
+    return pair ? 2 : 1;
 }
 
 int raw_big_enabled() {
@@ -1862,6 +2051,7 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
         CUtensorMap tm_check;
         MapBatch mb_check;
         g.out_rows = encode_output(&tm_check, target, *ov, &mb_check) ? 1 : 0;
+        g.out_v8 = g.out_rows && rows_aligned32(target, *ov) ? 1 : 0;  // narrowed per variant below
     }
     g.ob = make_decode(ov->b, ov->nb);
     g.om = make_decode(ov->m, ov->nm);
@@ -1913,6 +2103,7 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
             vbs.base = (uint8_t*)ws + L.bs_off;
             if (!encode_operand(&g.tmb, vb, true, 128) || !encode_operand(&g.tmbs, vbs, true, 128))
                 return set_last_error(PE_ERR_UNSUPPORTED);
+            g.out_v8 &= epi_v8_enabled(true);
             gemm_step(Cfg<256, true, 8, true, 0>{}, g);
         } else if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256 >= num_sms() &&
             wide_fp32_enabled()) {
@@ -1921,22 +2112,37 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
             vbs.base = (uint8_t*)ws + L.bs_off;
             if (!encode_operand(&g.tmb, vb, true, 256) || !encode_operand(&g.tmbs, vbs, true, 256))
                 return set_last_error(PE_ERR_UNSUPPORTED);
+            g.out_v8 &= epi_v8_enabled(false);
             gemm_step(Cfg<256, true, 8, false, 0>{}, g);
         } else if (g.a_pre && g.b_pre) {
+            g.out_v8 &= epi_v8_enabled(false);
             gemm_step(Cfg<128, true, 8, false, 0>{}, g);
         } else {
+            g.out_v8 &= epi_v8_enabled(false);
             gemm_step(Cfg<128, true>{}, g);
         }
     } else {
         // pairs halve each SM's operand traffic, which pays off where the
         // mainloop dominates (long K); output-bound short-K shapes stay single
         const bool pair = L.bn == 256 && g.K >= 512 && L.sk_q == 0 && pairs_enabled();
-        if (!encode_operand(&g.tma, va, false, 128) || !encode_operand(&g.tmb, vb, false, pair ? 128 : L.bn))
+        // two 128-byte contraction rows per stage (unsplit launches only: the
+        // split-K reductions count k-iterations of one row)
+        const int kb = (L.ksplit <= 1 && L.sk_q == 0) ? stage_rows(pair) : 1;
+        const int box_k = kb == 2 ? 128 : 0;
+        if (!encode_operand(&g.tma, va, false, 128, box_k) ||
+            !encode_operand(&g.tmb, vb, false, pair ? 128 : L.bn, box_k))
             return set_last_error(PE_ERR_UNSUPPORTED);
-        if (pair)
+        g.out_v8 &= epi_v8_enabled(pair);
+        if (pair && kb == 2)
+            gemm_step(Cfg<256, false, 8, true, 0, 2>{}, g);
+        else if (pair)
             gemm_step(Cfg<256, false, 8, true>{}, g);
+        else if (L.bn == 256 && kb == 2)
+            gemm_step(Cfg<256, false, 8, false, 0, 2>{}, g);
         else if (L.bn == 256)
             gemm_step(Cfg<256, false>{}, g);
+        else if (kb == 2)
+            gemm_step(Cfg<128, false, 8, false, 0, 2>{}, g);
         else
             gemm_step(Cfg<128, false>{}, g);
     }
@@ -1966,6 +2172,17 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
 }
 
 }  // namespace
+
+#ifdef PE_STALL_STATS
+// Diagnostic build only: copy (and clear) the per-CTA wait counters.
+extern "C" int pe_stall_stats(unsigned long long* host, int n) {
+    if (n > 1024 * 8) n = 1024 * 8;
+    if (cudaMemcpyFromSymbol(host, pe_stall, n * sizeof(unsigned long long)) != cudaSuccess) return -1;
+    static unsigned long long zero[1024 * 8];
+    if (cudaMemcpyToSymbol(pe_stall, zero, sizeof(zero)) != cudaSuccess) return -1;
+    return 0;
+}
+#endif
 
 // Self-test of the bounded-wait path: one CTA waits on an mbarrier that nothing
 // arrives on, through the same mbar_wait the GEMM pipeline uses, with a short

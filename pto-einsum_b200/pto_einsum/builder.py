@@ -487,7 +487,9 @@ class EinsumBuilder:
             inp0, inp1 = inp0.contiguous(), inp1.contiguous()
             if swap:
                 inp0, inp1 = inp1, inp0
-            out = torch.zeros(out_shape, dtype=torch.float32, device="cpu")
+            # every element is written by run_einsum (no zero fill: a parallel torch
+            # fill would leave its worker threads spinning against ours)
+            out = torch.empty(out_shape, dtype=torch.float32, device="cpu")
             if out.numel() == 0:
                 return out
             self.lib.run_einsum(inp0.data_ptr(), inp1.data_ptr(), out.data_ptr(), None)
