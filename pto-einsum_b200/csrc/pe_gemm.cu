@@ -919,14 +919,14 @@ bool rows_aligned32(const float* out, const OutView& o) {
     return true;
 }
 
-// Full-line epilogue stores: on by default for single-CTA tiles (output-bound
-// shapes gained 2-6%), off for CTA pairs (3% slower there: the pair mainloop
-// is operand-load bound and the shuffles lengthen the epilogue). PE_EPI_V8=0/1
+// Full-line epilogue stores: on by default (output-bound shapes gained 2-6%,
+// fp32 pairs included), off for fp16 CTA pairs (3% slower there: that
+// mainloop is operand-load bound and the shuffles lengthen the epilogue). PE_EPI_V8=0/1
 // forces either.
-int epi_v8_enabled(bool pair) {
+int epi_v8_enabled(bool fp16_pair) {
     const char* e = getenv("PE_EPI_V8");
     if (e && (e[0] == '0' || e[0] == '1')) return e[0] - '0';
-    return pair ? 0 : 1;
+    return fp16_pair ? 0 : 1;
 }
 
 Decode make_decode(const Axis* ax, int n) {
@@ -2103,7 +2103,7 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
             vbs.base = (uint8_t*)ws + L.bs_off;
             if (!encode_operand(&g.tmb, vb, true, 128) || !encode_operand(&g.tmbs, vbs, true, 128))
                 return set_last_error(PE_ERR_UNSUPPORTED);
-            g.out_v8 &= epi_v8_enabled(true);
+            g.out_v8 &= epi_v8_enabled(false);
             gemm_step(Cfg<256, true, 8, true, 0>{}, g);
         } else if (g.a_pre && g.b_pre && pl->L1 >= 256 && g.acc_slots <= 2 && tiles256 >= num_sms() &&
             wide_fp32_enabled()) {
