@@ -67,6 +67,9 @@ struct GemmArgs {
     int out_rows;    // output rows unit-stride with 16-byte aligned strides (full-sector stores)
     int out_v8;      // and 32-byte aligned rows: full-line 32-byte stores after a quad transpose
     int acc_slots;   // fp32: accumulator slots per tile (1, 2 or 4)
+    int fuse_b;      // fp32, 128-column single-CTA tiles: one N=256 MMA Ab x [Bb | Bs] and one
+                     // N=128 MMA As x Bb per k-step; B's small half lands right after B, A's
+                     // after it; two k-rotation slots of two 128-column halves (acc_slots = 4)
     int ksplit;      // work units per output tile (split-K), >= 1
     int kper;        // k-iterations per unit
     int sk_q;        // stream-K: k-iterations per CTA (group) over the flattened (tile, k) space; 0 = off
@@ -341,8 +344,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     load_a(sa, &g.tma);
                     load_b(sb, &g.tmb);
                     if constexpr (C::F32) {
-                        if (g.a_pre) load_a(sa + C::TX_BYTES, &g.tmas);
-                        if (g.b_pre) load_b(sb + C::TX_BYTES, &g.tmbs);
+                        // fused-B stages: [A][B][B small][A small]
+                        if (g.a_pre) load_a(sa + C::TX_BYTES + (g.fuse_b ? C::B_BYTES : 0), &g.tmas);
+                        if (g.b_pre) load_b(g.fuse_b ? sb + C::B_BYTES : sb + C::TX_BYTES, &g.tmbs);
                     }
                     if (++stage == C::STAGES) {
                         stage = 0;
@@ -361,6 +365,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         if (lane == 0 && rank == 0) {
             // ---------------- MMA issuer (pairs: the leader CTA only) ----------------
             const uint32_t idesc = make_idesc(C::F32 ? 2u : 0u, C::TM, C::BN, g.a_mn, g.b_mn);
+            const uint32_t idesc2 = make_idesc(2u, C::TM, 2 * C::BN, g.a_mn, g.b_mn);  // fused B: N = 2 BN
             // byte step of one UMMA_K slice and leading offsets of MN-major tiles
             const uint32_t a_kstep = g.a_mn ? (C::UMMA_K / 8) * 1024 : 32;
             const uint32_t b_kstep = g.b_mn ? (C::UMMA_K / 8) * 1024 : 32;
@@ -405,6 +410,20 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                         const uint64_t ad = smem_desc_sw128(sa + a_off, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = smem_desc_sw128(sb + b_off, b_lbo, b_sbo, b_lay);
                         const uint32_t accum = (kb - kb_lo >= S || ks > 0) ? 1u : 0u;
+                        if constexpr (C::F32 && !C::PAIR && C::BN == 128) {
+                            if (g.fuse_b) {
+                                // [Bb | Bs] is one 256-column operand (Bs follows B in the
+                                // stage with the same layout): D1 = Ab.Bb, D2 = Ab.Bs, then
+                                // D2 += As.Bb; k-steps alternate between two (D1, D2) pairs
+                                const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + C::B_BYTES + ks * a_kstep, a_lbo,
+                                                                     a_sbo, a_lay);
+                                const uint32_t dd = dbuf + (uint32_t)(((kb - kb_lo) & 1) * 2 * C::BN);
+                                const uint32_t acc1 = (kb - kb_lo >= 2 || ks > 0) ? 1u : 0u;
+                                mma_tf32(dd, ad, bd, idesc2, acc1);
+                                mma_tf32(dd + C::BN, ads, bd, idesc, 1u);
+                                continue;
+                            }
+                        }
                         if constexpr (C::F32) {
                             const uint64_t ads = smem_desc_sw128(sa + C::TX_BYTES + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t bds = smem_desc_sw128(sb + C::TX_BYTES + ks * b_kstep, b_lbo, b_sbo, b_lay);
@@ -472,7 +491,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
 #endif
             tc_fence_after();
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * S * C::BN);
-            const int nslots = S < kb_hi - kb_lo ? S : kb_hi - kb_lo;
+            // fused B: two 128-column halves per k-rotation slot, up to two slots
+            const int nslots = g.fuse_b ? 2 * min(2, kb_hi - kb_lo) : (S < kb_hi - kb_lo ? S : kb_hi - kb_lo);
             const int bidx = i + sp * g.nbatch;  // output batch (split-K: partial slab sp)
             const int mrow = m0 + q * 32;
             const int m = mrow + lane;
@@ -680,7 +700,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                     break;
                 }
                 uint4* big = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES);
-                uint4* small = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES + C::TX_BYTES);
+                // small halves mirror [A][B] at TX_BYTES; fused-B stages hold [B small][A small]
+                uint4* small_a = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES + C::TX_BYTES +
+                                                          (g.fuse_b ? C::B_BYTES : 0));
+                uint4* small_b = reinterpret_cast<uint4*>(smem + stage * C::STAGE_BYTES + C::TX_BYTES -
+                                                          (g.fuse_b ? C::A_BYTES : 0));
 #pragma unroll 4
                 for (int j = jlo + st; j < jhi; j += 128) {
                     uint4 x = big[j];
@@ -691,7 +715,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                                            __uint_as_float(x.z) - __uint_as_float(h.z),
                                            __uint_as_float(x.w) - __uint_as_float(h.w));
                     if (!g.raw_big) big[j] = h;
-                    small[j] = *reinterpret_cast<uint4*>(&s);
+                    (j < C::A_BYTES / 16 ? small_a : small_b)[j] = *reinterpret_cast<uint4*>(&s);
                 }
                 fence_proxy_async_smem();
                 mbar_arrive(split(stage));
@@ -1089,6 +1113,12 @@ int stage_rows(bool pair) {
     const char* e = getenv("PE_GEMM_KB");
     if (e && (e[0] == '1' || e[0] == '2')) return e[0] - '0';
     return pair ? 2 : 1;
+}
+
+// fp32 fused-B MMAs on 128-column tiles (PE_GEMM_FUSEB=0 keeps three N=128 MMAs)
+int fuse_b_enabled() {
+    const char* e = getenv("PE_GEMM_FUSEB");
+    return (e && e[0] == '0') ? 0 : 1;
 }
 
 int raw_big_enabled() {
@@ -2114,12 +2144,17 @@ int build_program(const pe_contract_plan& plan, const Lowered& L, const void* in
                 return set_last_error(PE_ERR_UNSUPPORTED);
             g.out_v8 &= epi_v8_enabled(false);
             gemm_step(Cfg<256, true, 8, false, 0>{}, g);
-        } else if (g.a_pre && g.b_pre) {
-            g.out_v8 &= epi_v8_enabled(false);
-            gemm_step(Cfg<128, true, 8, false, 0>{}, g);
         } else {
+            // 128-column tiles: fused-B MMAs from two k-steps on (both rotation slots used)
+            if (g.acc_slots >= 2 && fuse_b_enabled()) {
+                g.fuse_b = 1;
+                g.acc_slots = 4;
+            }
             g.out_v8 &= epi_v8_enabled(false);
-            gemm_step(Cfg<128, true>{}, g);
+            if (g.a_pre && g.b_pre)
+                gemm_step(Cfg<128, true, 8, false, 0>{}, g);
+            else
+                gemm_step(Cfg<128, true>{}, g);
         }
     } else {
         // pairs halve each SM's operand traffic, which pays off where the

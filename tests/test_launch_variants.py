@@ -5,8 +5,10 @@ default parity suites do not reach:
   PE_GEMM_KB   1 or 2 contraction rows (128 bytes each) per pipeline stage
   PE_EPI_V8    full-line (32-byte) epilogue stores on / off
   PE_GEMM_PDL  programmatic dependent launch on / off
-None of them changes the order of the tensor-core accumulation, so every
-variant must reproduce the default result bit for bit. Each variant runs in a
+  PE_GEMM_FUSEB  fp32 fused-B MMAs on / off (changes the accumulation split:
+                 compared with the oracle tolerance, not bit for bit)
+The first three do not change the order of the tensor-core accumulation, so
+those variants must reproduce the default result bit for bit. Each variant runs in a
 child process (the switches are read once per process) on the same seeded
 inputs; the default run is also checked against a float64 torch.einsum on
 the GPU (the CPU-oracle parity of these paths is covered by the parity suites).
@@ -38,6 +40,7 @@ cases = [
     ("bij,bkj->bik", (8, 1024, 512), (8, 1024, 512), torch.float16),    # CTA pairs, K-major B
     ("bshd,bthd->bsht", (2, 256, 8, 64), (2, 320, 8, 64), torch.float16),  # single CTAs, permuted store
     ("tn,sn->ts", (1024, 128), (1024, 128), torch.float32),            # 3xTF32
+    ("ts,sp->tp", (512, 4096), (4096, 128), torch.float32),            # 3xTF32 fused B, stream-K
     ("ij,jk->ik", (300, 200), (200, 520), torch.float16),              # ragged tiles
 ]
 out = {{}}
@@ -63,7 +66,7 @@ VARIANTS = [
 def _run_child(env_extra, path):
     code = CHILD.format(pkg=os.path.join(REPO, "pto-einsum_b200"), repo=REPO, tests=HERE, path=path)
     env = dict(os.environ)
-    for k in ("PE_GEMM_KB", "PE_EPI_V8", "PE_GEMM_PDL"):
+    for k in ("PE_GEMM_KB", "PE_EPI_V8", "PE_GEMM_PDL", "PE_GEMM_FUSEB"):
         env.pop(k, None)
     env.update(env_extra)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
@@ -91,6 +94,15 @@ def test_switch_variants_bit_identical(tmp_path):
         got = _run_child(v, str(tmp_path / f"v{j}.npz"))
         for key in base:
             np.testing.assert_array_equal(got[key], base[key], err_msg=f"variant {v}, case {key}")
+    # three separate MMAs instead of the fused-B pair: same tolerance as the default
+    got = _run_child({"PE_GEMM_FUSEB": "0"}, str(tmp_path / "nofuse.npz"))
+    for k, (eq, s0, s1, dt) in enumerate(cases):
+        dt = getattr(torch, dt)
+        a = seeded(eval(s0), dt, 500 + k, "randn").cuda().double()
+        b = seeded(eval(s1), dt, 600 + k, "randn").cuda().double()
+        ref = torch.einsum(eq, a, b)
+        g = torch.from_numpy(got[str(k)]).cuda().double()
+        assert ((g - ref).norm() / ref.norm()).item() <= TOL[dt], eq
 
 
 @pytest.mark.gpu
