@@ -5,9 +5,10 @@ default parity suites do not reach:
   PE_GEMM_KB   1 or 2 contraction rows (128 bytes each) per pipeline stage
   PE_EPI_V8    full-line (32-byte) epilogue stores on / off
   PE_GEMM_PDL  programmatic dependent launch on / off
+  PE_EPI_WARPS_PAIR  4 or 8 epilogue warps on fp16 CTA pairs
   PE_GEMM_FUSEB  fp32 fused-B MMAs on / off (changes the accumulation split:
                  compared with the oracle tolerance, not bit for bit)
-The first three do not change the order of the tensor-core accumulation, so
+The first four do not change the order of the tensor-core accumulation, so
 those variants must reproduce the default result bit for bit. Each variant runs in a
 child process (the switches are read once per process) on the same seeded
 inputs; the default run is also checked against a float64 torch.einsum on
@@ -60,13 +61,15 @@ VARIANTS = [
     {"PE_EPI_V8": "0"},
     {"PE_EPI_V8": "1"},
     {"PE_GEMM_PDL": "0"},
+    {"PE_EPI_WARPS_PAIR": "4"},
+    {"PE_EPI_WARPS_PAIR": "8"},
 ]
 
 
 def _run_child(env_extra, path):
     code = CHILD.format(pkg=os.path.join(REPO, "pto-einsum_b200"), repo=REPO, tests=HERE, path=path)
     env = dict(os.environ)
-    for k in ("PE_GEMM_KB", "PE_EPI_V8", "PE_GEMM_PDL", "PE_GEMM_FUSEB"):
+    for k in ("PE_GEMM_KB", "PE_EPI_V8", "PE_GEMM_PDL", "PE_GEMM_FUSEB", "PE_EPI_WARPS_PAIR"):
         env.pop(k, None)
     env.update(env_extra)
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
